@@ -1,0 +1,462 @@
+#!/usr/bin/env python3
+"""Benchmark of the fused relu(A @ B + bias) ("mbr") hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--mode fp32|tf32|bf16|fp32_exact]
+                    [--m M --n N --k K] [--impl ours|reference]
+
+One step = one call of the library's fused operator (tforge_mbr, the C-ABI of
+include/tforge.h) on one batch: A (M x K), B (K x N), bias (N) -> out (M x N), f32,
+U[-1, 1] synthetic inputs.  Default workload: BASELINE config 2, M = N = K = 2048 in
+the fp32-accurate (3xTF32) mode.  With N GPUs (torchrun, one rank per GPU, NCCL) each
+rank owns a 2048-row shard of an (N * 2048) x 2048 x 2048 problem: A rows are generated
+per rank, B and bias are broadcast once from rank 0 over NCCL before timing, outputs stay
+sharded (weak scaling; no collective inside the timed region).
+
+Timing: W untimed warm-up steps; then K steps between a barrier + synchronize on both
+sides; before every step a 256 MiB buffer is written to flush L2 (126 MB), outside the
+step's CUDA-event pair on the launching stream; the step times are summed; the max over
+ranks is reported.  `value` = total FLOP of all ranks / that time (2 M N K per call, the
+reference's convention, python/tforge_cpu.py:154-157).
+
+Also reported: `roofline` of the GEMM kernel against the measured bf16 peak scaled to the
+mode (TF32 = bf16 / 2, 3xTF32 = TF32 / 3); `cpu_baseline` (the CPU restatement of the
+reference kernel, pinned to the reference's published numerics, timed on the host cores
+over row slices); `e2e` through the C-ABI with pinned host buffers and the copies in the
+timed region; `clocks` sampled through NVML during the timed region.
+
+`--impl reference` times the reference's own CPU implementation of the path (its MLIR
+pipeline cannot be built here, so the pinned C restatement stands in) on all host
+threads, and prints the same JSON keys with "impl": "reference".
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import pathlib
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fused MBR TFLOP/s (2048^3 fp32, device-timed), % tensor peak, 1/2/4/8 B200"
+FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--mode", default="fp32", choices=["fp32", "tf32", "bf16", "fp32_exact"])
+    ap.add_argument("--m", type=int, default=2048, help="rows per GPU")
+    ap.add_argument("--n", type=int, default=2048)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------- CPU restatement timing
+def cpu_restatement_tflops(m, n, k, seconds=10.0, max_reps=50):
+    """Time the CPU restatement of the reference kernel (oracle/, pinned to the reference's
+    published numerics) on all host threads, one single-threaded call per row slice, the
+    way the single-threaded reference kernel would use every core."""
+    import concurrent.futures as cf
+
+    import numpy as np
+
+    from tests import oracle_lib
+    from tensorforge_b200 import tforge_cpu as tc
+
+    threads = host_threads()
+    ins = tc.make_inputs("mbr", m, n, k, 0)
+    a, b, bias = ins["a"], ins["b"], ins["bias"]
+    out = np.empty((m, n), dtype=np.float32)
+    lib = oracle_lib._lib
+    rows = [(i * m // threads, (i + 1) * m // threads) for i in range(threads)]
+    rows = [r for r in rows if r[1] > r[0]]
+
+    def part(r):
+        r0, r1 = r
+        lib.oracle_gemm(1, a[r0:].ctypes.data, b.ctypes.data, bias.ctypes.data, out[r0:].ctypes.data,
+                        r1 - r0, n, k, 1)
+
+    times = []
+    with cf.ThreadPoolExecutor(max_workers=len(rows)) as ex:
+        list(ex.map(part, rows))  # warm-up
+        t_end = time.perf_counter() + seconds / max(1, len(rows)) * 1.0
+        while len(times) < max_reps:
+            t0 = time.perf_counter()
+            list(ex.map(part, rows))
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() > t_end and len(times) >= 3:
+                break
+    med = statistics.median(times)
+    return 2.0 * m * n * k / med / 1e12, len(rows), len(times), med
+
+
+def reference_arm(args):
+    """--impl reference: the reference's CPU implementation of the path on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    subprocess_build_oracle()
+    import numpy as np  # noqa: F401
+
+    m, n, k = args.m, args.n, args.k
+    from tests import oracle_lib
+    from tensorforge_b200 import tforge_cpu as tc
+    import concurrent.futures as cf
+
+    threads = host_threads()
+    ins = tc.make_inputs("mbr", m, n, k, 0)
+    a, b, bias = ins["a"], ins["b"], ins["bias"]
+    import numpy as np
+
+    out = np.empty((m, n), dtype=np.float32)
+    rows = [(i * m // threads, (i + 1) * m // threads) for i in range(threads)]
+    rows = [r for r in rows if r[1] > r[0]]
+
+    def part(r):
+        r0, r1 = r
+        oracle_lib._lib.oracle_gemm(1, a[r0:].ctypes.data, b.ctypes.data, bias.ctypes.data,
+                                    out[r0:].ctypes.data, r1 - r0, n, k, 1)
+
+    step_t = []
+    with cf.ThreadPoolExecutor(max_workers=len(rows)) as ex:
+        for _ in range(args.warmup):
+            list(ex.map(part, rows))
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            list(ex.map(part, rows))
+            step_t.append(time.perf_counter() - t0)
+    total = sum(step_t)
+    value = 2.0 * m * n * k * args.steps / total / 1e12
+    res = tc.check_output("mbr", ins, out, "fp32_exact", rows=np.arange(0, m, max(1, m // 64)))
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"mbr {m}x{n}x{k} f32, U[-1,1] seed 0 (BASELINE config 2)",
+                       "implementation": "C restatement of the reference's tforge-cpu-pipeline kernel "
+                                         "(6x16 register tiles, sequential-k FMA; the MLIR pipeline that "
+                                         "generates the real kernel is not buildable here)",
+                       "err_over_bound": res["err_over_bound"]},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": len(rows), "kind": "port",
+                             "sample": f"the full {m}x{n}x{k} problem per step, {len(rows)} row slices, "
+                                       "one single-threaded call each"},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def subprocess_build_oracle():
+    import subprocess
+
+    if not (ROOT / "oracle" / "build" / "liboracle.so").exists():
+        subprocess.run(["make", "-C", str(ROOT / "oracle")], check=True, capture_output=True)
+
+
+# ---------------------------------------------------------------- clocks (NVML)
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons through NVML in a thread."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index: int, period_s: float = 0.01):
+        self.samples, self.period, self.stop_ev = [], period_s, threading.Event()
+        self.ok = False
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self.nv, self.h = nv, nv.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: clocks reported as unavailable
+            self.err = str(e)
+        self.th = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((sm, pw, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.th.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.stop_ev.set()
+        if self.ok:
+            self.th.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable: " + self.err}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        reasons = set()
+        for _, _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": self.max_mhz,
+                "power_w_median": statistics.median(s[1] for s in self.samples),
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- roofline inputs
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+def profiled_traffic(kernel: str, mode: str, m: int, n: int, k: int):
+    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary, or None."""
+    path = ROOT / "profiles" / f"gemm_tcgen05_{mode}_mbr_{m}x{n}x{k}.md"
+    if not path.exists():
+        return None
+    mt = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+    return float(mt.group(1)) if mt else None
+
+
+# ---------------------------------------------------------------- our arm
+def ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from tensorforge_b200 import _lib, tforge_cpu as tc, tforge_gpu as tg
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    L = _lib.lib()
+    _lib.check(L.tforge_set_device(local))
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    m, n, k, mode = args.m, args.n, args.k, args.mode
+    # Inputs: A rows are this rank's shard (seed offset by rank); B and bias from rank 0.
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    A = torch.empty((m, k), device=dev, dtype=torch.float32).uniform_(-1, 1, generator=g)
+    B = torch.empty((k, n), device=dev, dtype=torch.float32)
+    bias = torch.empty((n,), device=dev, dtype=torch.float32)
+    if rank == 0:
+        g0 = torch.Generator(device=dev)
+        g0.manual_seed(7)
+        B.uniform_(-1, 1, generator=g0)
+        bias.uniform_(-1, 1, generator=g0)
+    bcast_ms = None
+    if world > 1:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        dist.broadcast(B, src=0)
+        dist.broadcast(bias, src=0)
+        torch.cuda.synchronize()
+        bcast_ms = 1e3 * (time.perf_counter() - t0)
+    out = torch.empty((m, n), device=dev, dtype=torch.float32)
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step():
+        rc = L.tforge_mbr(A.data_ptr(), B.data_ptr(), bias.data_ptr(), out.data_ptr(), m, n, k,
+                          _lib.MODES[mode], sp)
+        if rc:
+            raise _lib.TforgeError(rc, "tforge_mbr")
+
+    launch = _lib.describe("mbr", m, n, k, mode)
+    launches_per_step = 1 + (2 if mode == "bf16" else 0)  # bf16 mode converts A and B first
+
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        step()
+    torch.cuda.synchronize()
+    assert _lib.device_status(sp) == 0
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    status = _lib.device_status(sp)
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    flops_rank = 2.0 * m * n * k
+    value = world * flops_rank * args.steps / (total_ms * 1e-3) / 1e12
+
+    # Correctness of the timed output (seeded row subset vs FP64, the reference's bound).
+    rows = np.arange(0, m, max(1, m // 64))
+    ins = {"a": A.cpu().numpy(), "b": B.cpu().numpy(), "bias": bias.cpu().numpy()}
+    res = tc.check_output("mbr", ins, out.cpu().numpy(), mode, rows=rows)
+
+    result = None
+    if rank == 0:
+        peaks = measured_peaks()
+        peak, basis = tg.tensor_roofline_tflops(mode, peaks)
+        achieved = flops_rank / (statistics.mean(step_ms) * 1e-3) / 1e12
+        traffic = profiled_traffic(launch["kernel"], mode, m, n, k)
+        roof = None
+        if peak:
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": traffic,
+                    "kernel": launch["kernel"],
+                    "peak_basis": (f"{basis} bf16 GEMM peak {peaks.get('bf16_tflops', 1590.0)} TFLOP/s (burst, "
+                                   "MEASURED_PEAKS.json) scaled to the mode: TF32 = bf16/2, 3xTF32 = TF32/3"),
+                    "algorithmic_flop_per_launch": flops_rank}
+        comparators = cublas_comparator(m, n, k, A, B, bias, flush, stream) if mode in ("fp32", "fp32_exact") else {}
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            subprocess_build_oracle()
+            v, cores, reps, med = cpu_restatement_tflops(m, n, k)
+            cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                   "sample": f"full {m}x{n}x{k} mbr, {reps} timed reps (median {med:.3f} s), {cores} row slices "
+                             "each one single-threaded call of the C restatement of the reference kernel"}
+        e2e = None if args.no_e2e else e2e_measure(L, _lib, m, n, k, mode, A, B, bias, world, dev)
+        result = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                  "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+                  "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                  "data": "synthetic",
+                  "config": {"workload": f"mbr relu(A@B+bias) {m}x{n}x{k} per GPU, mode {mode}"
+                                         f"{' (3xTF32 split products, f32 accumulate)' if mode == 'fp32' else ''}, "
+                                         "A/B/bias U[-1,1]",
+                             "M_total": m * world, "N": n, "K": k, "mode": mode,
+                             "l2": "flushed before every step (256 MiB write outside the step's events)",
+                             "parallelism": f"M-sharded rows over {world} GPU(s); B and bias NCCL-broadcast once "
+                                            "before timing; outputs stay sharded",
+                             "kernel": launch["kernel"], "tile": launch["tile"], "stages": launch["stages"],
+                             "broadcast_ms": bcast_ms,
+                             "err_over_bound": res["err_over_bound"], "check_pass": bool(res["pass"]),
+                             "device_status": status},
+                  "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+                  "gpu_launches": launches_per_step * args.steps,
+                  "comparators": comparators}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def cublas_comparator(m, n, k, A, B, bias, flush, stream):
+    """The reference's comparator on the same GPU: cuBLAS SGEMM (FP32, no TF32) followed by
+    a separate bias + ReLU pass (runners/gpu/tforge-gpu-bench.cu:303-318)."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        C_ = torch.empty((m, n), device=A.device, dtype=torch.float32)
+
+        def run():
+            torch.matmul(A, B, out=C_)
+            C_.add_(bias).clamp_(min=0.0)
+
+        for _ in range(5):
+            run()
+        ts = []
+        for i in range(20):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        med = statistics.median(ts)
+        return {"cublas_sgemm_plus_bias_relu": {"tflops": 2.0 * m * n * k / (med * 1e-3) / 1e12, "ms": med}}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def e2e_measure(L, _lib, m, n, k, mode, A, B, bias, world, dev, steps=20, warmup=3):
+    """The same operator through the C-ABI on HOST buffers: pinned H2D of A, B and bias, the
+    fused kernel, D2H of the output, all inside the timed region (CUDA events)."""
+    import torch
+
+    hA, hB, hb = A.cpu().pin_memory(), B.cpu().pin_memory(), bias.cpu().pin_memory()
+    hO = torch.empty((m, n), dtype=torch.float32).pin_memory()
+    dA, dB, db, dO = torch.empty_like(A), torch.empty_like(B), torch.empty_like(bias), torch.empty((m, n), device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    h2d = hA.numel() * 4 + hB.numel() * 4 + hb.numel() * 4
+    d2h = hO.numel() * 4
+
+    def one():
+        for dst, src, nb in ((dA, hA, hA.numel() * 4), (dB, hB, hB.numel() * 4), (db, hb, hb.numel() * 4)):
+            _lib.check(L.tforge_memcpy_h2d(dst.data_ptr(), src.data_ptr(), nb, sp), "H2D")
+        _lib.check(L.tforge_mbr(dA.data_ptr(), dB.data_ptr(), db.data_ptr(), dO.data_ptr(), m, n, k,
+                                _lib.MODES[mode], sp), "tforge_mbr")
+        _lib.check(L.tforge_memcpy_d2h(hO.data_ptr(), dO.data_ptr(), d2h, sp), "D2H")
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "steps": steps,
+            "path": "tforge_memcpy_h2d x3 -> tforge_mbr -> tforge_memcpy_d2h (pinned host buffers), rank 0"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,571 @@
+// tf_api.cu -- the C-ABI (include/tforge.h): argument checks, the per-shape dispatch
+// table, TMA tensor-map encoding, the device status word and small device helpers.
+//
+// The dispatch table replaces the reference's analytical cost model and autotuner
+// (python/costmodel.py:49-97, bench/stage9_costmodel.py:63-154): the tile choice is a
+// function of (mode, M, N, K) over the instantiated tcgen05 configurations.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/tforge.h"
+#include "tf_internal.h"
+
+using namespace tf;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_wait_limit_ns{1000000000ull};
+std::atomic<int> g_debug_skip{0};
+std::mutex g_cfg_mu;
+tforge_config g_cfg{};  // kernel == 0: use the table
+
+int cuda_fail(cudaError_t e, const char *what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return TFORGE_ERR_CUDA;
+}
+
+// ---- cuTensorMapEncodeTiled through the runtime's driver entry point -----------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D row-major tensor [rows x cols] with pitch `ld` elements; box = {box_cols, box_rows};
+// 128-byte swizzle (16-byte atoms, or 32-byte atoms with `atom32`, the layout the tensor
+// cores require for N-contiguous 32-bit operands); out-of-range elements read as zero.
+int make_tmap(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols, int64_t ld,
+              uint32_t box_cols, uint32_t box_rows, bool atom32 = false) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    g_last_error = "cuTensorMapEncodeTiled unavailable";
+    return TFORGE_ERR_CUDA;
+  }
+  const int esz = bf16 ? 2 : 4;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                   const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_error = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+    return TFORGE_ERR_CUDA;
+  }
+  return TFORGE_OK;
+}
+
+// ---- per-device status word ------------------------------------------------------------
+constexpr int kMaxDev = 64;
+uint32_t *g_status[kMaxDev] = {};
+std::mutex g_status_mu;
+
+int status_word(uint32_t **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDev) return TFORGE_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (!g_status[dev]) {
+    void *p = nullptr;
+    e = cudaMalloc(&p, 256);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(status)");
+    e = cudaMemset(p, 0, 256);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+    g_status[dev] = static_cast<uint32_t *>(p);
+  }
+  *out = g_status[dev];
+  return TFORGE_OK;
+}
+
+// ---- per-device scratch pool -------------------------------------------------------------
+// Stream-ordered scratch (bf16 copies of f32 operands) comes from a pool the library owns,
+// so concurrent streams never share a buffer and freed memory stays mapped for reuse
+// (the release threshold is unlimited); the caller's default pool is left untouched.
+cudaMemPool_t g_pool[kMaxDev] = {};
+
+int scratch_pool(cudaMemPool_t *out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDev) return TFORGE_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (!g_pool[dev]) {
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    e = cudaMemPoolCreate(&pool, &props);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemPoolCreate");
+    uint64_t keep = UINT64_MAX;
+    e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemPoolSetAttribute");
+    g_pool[dev] = pool;
+  }
+  *out = g_pool[dev];
+  return TFORGE_OK;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+bool overlaps(const void *a, size_t abytes, const void *b, size_t bbytes) {
+  if (!a || !b || !abytes || !bbytes) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + bbytes && b0 < a0 + abytes;
+}
+
+size_t span_bytes(int64_t rows, int64_t cols, int64_t ld, int esz) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return (size_t)((rows - 1) * ld + cols) * esz;
+}
+
+// ---- dispatch table ------------------------------------------------------------------------
+enum KernelKind { K_TC = 1, K_SIMT = 2 };
+
+struct Choice {
+  int kind;
+  TcConfig tc;
+};
+
+// Number of CTAs of an M x N problem for a BN-wide tile (BM = 128).
+int64_t ctas(int64_t M, int64_t N, int bn) { return ((M + 127) / 128) * ((N + bn - 1) / bn); }
+
+TcConfig table_tc(int prec, int64_t M, int64_t N, int64_t K) {
+  (void)K;
+  // Prefer the widest tile (least operand traffic per FLOP) unless a narrower one fills
+  // the 148 SMs noticeably better: compare the fraction of the last wave that is busy.
+  const int bns[3] = {256, 128, 64};
+  const int st[3][3] = {{4, 6, 8}, {2, 3, 4}, {4, 6, 8}};  // [prec][bn index]
+  int best = 0;
+  double best_score = -1;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t c = ctas(M, N, bns[i]);
+    const double waves = (double)c / 148.0;
+    const double eff = waves / (double)((c + 147) / 148);  // SM-slot utilisation
+    // Columns of the last N tile that hold no output are wasted MMA work.
+    const double n_eff = (double)N / (double)(((N + bns[i] - 1) / bns[i]) * bns[i]);
+    // Narrower tiles cost operand bandwidth: weight by a per-width efficiency guess.
+    const double width_eff = bns[i] == 256 ? 1.0 : (bns[i] == 128 ? 0.9 : 0.75);
+    const double score = eff * n_eff * width_eff;
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = i;
+    }
+  }
+  return TcConfig{prec, bns[best], st[prec][best]};
+}
+
+Choice choose(int mode, int64_t M, int64_t N, int64_t K, bool tma_ok) {
+  Choice c{K_SIMT, {}};
+  if (mode == TFORGE_MODE_FP32_EXACT || K == 0 || !tma_ok) return c;
+  // 3xTF32 carries about 2^-20 relative error per product independent of K, while the
+  // fp32 bound gamma_{K+1} shrinks with K; below K = 16 the exact kernel is used instead.
+  if (mode == TFORGE_MODE_FP32 && K < 16) return c;
+  const int prec = mode == TFORGE_MODE_FP32 ? PREC_X3 : (mode == TFORGE_MODE_TF32 ? PREC_TF32 : PREC_BF16);
+  c.kind = K_TC;
+  c.tc = table_tc(prec, M, N, K);
+  std::lock_guard<std::mutex> lk(g_cfg_mu);
+  if (g_cfg.kernel == 2) {
+    c.kind = K_SIMT;
+  } else if (g_cfg.kernel == 1) {
+    TcConfig f{prec, g_cfg.bn ? g_cfg.bn : c.tc.bn, g_cfg.stages ? g_cfg.stages : c.tc.stages};
+    if (tc_config_supported(f)) c.tc = f;
+    else c.kind = -1;
+  }
+  return c;
+}
+
+int check_gemm(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *ldc) {
+  if (!a) return TFORGE_ERR_NULL;
+  if (a->workload < TFORGE_MATMUL || a->workload > TFORGE_MATMUL_ADD) return TFORGE_ERR_MODE;
+  if (a->mode < TFORGE_MODE_FP32 || a->mode > TFORGE_MODE_FP32_EXACT) return TFORGE_ERR_MODE;
+  if ((a->a_dtype != TFORGE_F32 && a->a_dtype != TFORGE_BF16) ||
+      (a->b_dtype != TFORGE_F32 && a->b_dtype != TFORGE_BF16))
+    return TFORGE_ERR_MODE;
+  if ((a->a_dtype == TFORGE_BF16 || a->b_dtype == TFORGE_BF16) && a->mode != TFORGE_MODE_BF16)
+    return TFORGE_ERR_MODE;
+  if (a->M < 0 || a->N < 0 || a->K < 0) return TFORGE_ERR_SHAPE;
+  if (a->M > INT32_MAX || a->N > INT32_MAX || a->K > INT32_MAX) return TFORGE_ERR_SHAPE;
+  *lda = a->lda ? a->lda : a->K;
+  *ldb = a->ldb ? a->ldb : a->N;
+  *ldc = a->ldc ? a->ldc : a->N;
+  if (*lda < a->K || *ldb < a->N || *ldc < a->N) return TFORGE_ERR_SHAPE;
+  if (a->M == 0 || a->N == 0) return TFORGE_OK;
+  if (!a->out) return TFORGE_ERR_NULL;
+  if (a->K > 0 && (!a->A || !a->B)) return TFORGE_ERR_NULL;
+  if (a->workload == TFORGE_MBR && !a->bias) return TFORGE_ERR_NULL;
+  if (a->workload == TFORGE_MATMUL_ADD && !a->C_res) return TFORGE_ERR_NULL;
+  const int ea = a->a_dtype == TFORGE_BF16 ? 2 : 4, eb = a->b_dtype == TFORGE_BF16 ? 2 : 4;
+  if (!aligned(a->A, ea) || !aligned(a->B, eb) || !aligned(a->out, 4) || !aligned(a->bias, 4) ||
+      !aligned(a->C_res, 4))
+    return TFORGE_ERR_ALIGN;
+  const size_t ob = span_bytes(a->M, a->N, *ldc, 4);
+  if (overlaps(a->out, ob, a->A, span_bytes(a->M, a->K, *lda, ea)) ||
+      overlaps(a->out, ob, a->B, span_bytes(a->K, a->N, *ldb, eb)) ||
+      (a->workload == TFORGE_MBR && overlaps(a->out, ob, a->bias, (size_t)a->N * 4)) ||
+      (a->workload == TFORGE_MATMUL_ADD && overlaps(a->out, ob, a->C_res, ob)))
+    return TFORGE_ERR_ALIAS;
+  return TFORGE_OK;
+}
+
+// TMA needs 16-byte-aligned bases and pitches; the vector epilogue needs 16-byte rows.
+bool tma_compatible(const tforge_gemm_args *a, int64_t lda, int64_t ldb, int64_t ldc) {
+  const int ea = a->a_dtype == TFORGE_BF16 ? 2 : 4, eb = a->b_dtype == TFORGE_BF16 ? 2 : 4;
+  if ((lda * ea) % 16 || (ldb * eb) % 16 || (ldc * 4) % 16) return false;
+  if (a->mode == TFORGE_MODE_BF16 && ((lda * 2) % 16 || (ldb * 2) % 16)) return false;
+  if (!aligned(a->A, 16) || !aligned(a->B, 16) || !aligned(a->out, 16)) return false;
+  if (a->workload == TFORGE_MBR && !aligned(a->bias, 16)) return false;
+  if (a->workload == TFORGE_MATMUL_ADD && !aligned(a->C_res, 16)) return false;
+  if (a->N % 4) return false;
+  return true;
+}
+
+int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const void *B,
+           bool bf16, int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t st) {
+  const int esz = bf16 ? 2 : 4;
+  const uint32_t bk = 128 / esz;  // K elements per stage
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap(&tmA, A, bf16, a->M, a->K, lda, bk, 128);
+  if (rc) return rc;
+  rc = make_tmap(&tmB, B, bf16, a->K, a->N, ldb, 128 / esz, bk, /*atom32=*/!bf16);
+  if (rc) return rc;
+  TcParams p{};
+  p.bias = a->bias;
+  p.cres = a->C_res;
+  p.out = a->out;
+  p.M = (int32_t)a->M;
+  p.N = (int32_t)a->N;
+  p.K = (int32_t)a->K;
+  p.ldc = ldc;
+  rc = status_word(&p.status);
+  if (rc) return rc;
+  p.limit_ns = g_wait_limit_ns.load();
+  p.debug_skip = g_debug_skip.load();
+  const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
+  cudaError_t e = launch_gemm_tc(cfg, epi, tmA, tmB, p, st);
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
+  return TFORGE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tforge_gemm(const tforge_gemm_args *a, void *stream) {
+  int64_t lda, ldb, ldc;
+  int rc = check_gemm(a, &lda, &ldb, &ldc);
+  if (rc) return rc;
+  if (a->M == 0 || a->N == 0) return TFORGE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
+  const bool f32_in = a->a_dtype == TFORGE_F32 && a->b_dtype == TFORGE_F32;
+  const Choice c = choose(a->mode, a->M, a->N, a->K, tma_compatible(a, lda, ldb, ldc));
+  if (c.kind < 0) return TFORGE_ERR_UNSUPPORTED;
+  if (c.kind == K_SIMT) {
+    if (!f32_in) return TFORGE_ERR_UNSUPPORTED;  // bf16 operands need the tensor-core path
+    const float *aux = a->workload == TFORGE_MBR ? a->bias : a->C_res;
+    cudaError_t e = launch_gemm_simt(epi, static_cast<const float *>(a->A),
+                                     static_cast<const float *>(a->B), aux, a->out, a->M, a->N, a->K,
+                                     lda, ldb, ldc, st);
+    return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "SIMT GEMM launch");
+  }
+  if (c.tc.prec != PREC_BF16) return run_tc(a, c.tc, a->A, a->B, false, lda, ldb, ldc, st);
+
+  // BF16 mode: f32 operands are rounded to bf16 into stream-ordered scratch first.
+  const void *A = a->A, *B = a->B;
+  void *scratch = nullptr;
+  int64_t la = lda, lb = ldb;
+  const size_t abytes = a->a_dtype == TFORGE_F32 ? (size_t)a->M * a->K * 2 : 0;
+  const size_t bbytes = a->b_dtype == TFORGE_F32 ? (size_t)a->K * a->N * 2 : 0;
+  if (abytes + bbytes) {
+    cudaMemPool_t pool = nullptr;
+    rc = scratch_pool(&pool);
+    if (rc) return rc;
+    cudaError_t e = cudaMallocFromPoolAsync(&scratch, abytes + bbytes + 256, pool, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocFromPoolAsync(bf16 scratch)");
+    uint16_t *sa = static_cast<uint16_t *>(scratch);
+    uint16_t *sb = reinterpret_cast<uint16_t *>(static_cast<char *>(scratch) + ((abytes + 255) & ~size_t(255)));
+    if (abytes) {
+      // Packed copy of a possibly pitched A: convert row blocks when pitched.
+      if (lda == a->K) e = launch_convert_bf16(static_cast<const float *>(a->A), sa, a->M * a->K, st);
+      else
+        for (int64_t r = 0; r < a->M && e == cudaSuccess; ++r)
+          e = launch_convert_bf16(static_cast<const float *>(a->A) + r * lda, sa + r * a->K, a->K, st);
+      A = sa;
+      la = a->K;
+    }
+    if (bbytes && e == cudaSuccess) {
+      if (ldb == a->N) e = launch_convert_bf16(static_cast<const float *>(a->B), sb, a->K * a->N, st);
+      else
+        for (int64_t r = 0; r < a->K && e == cudaSuccess; ++r)
+          e = launch_convert_bf16(static_cast<const float *>(a->B) + r * ldb, sb + r * a->N, a->N, st);
+      B = sb;
+      lb = a->N;
+    }
+    if (e != cudaSuccess) {
+      cudaFreeAsync(scratch, st);
+      return cuda_fail(e, "bf16 conversion");
+    }
+  }
+  if ((la * 2) % 16 || (lb * 2) % 16) {
+    if (scratch) cudaFreeAsync(scratch, st);
+    // bf16 rows must be 16-byte multiples for TMA: K and N multiples of 8.
+    const float *aux = a->workload == TFORGE_MBR ? a->bias : a->C_res;
+    if (!f32_in) return TFORGE_ERR_UNSUPPORTED;
+    cudaError_t e = launch_gemm_simt(epi, static_cast<const float *>(a->A),
+                                     static_cast<const float *>(a->B), aux, a->out, a->M, a->N,
+                                     a->K, lda, ldb, ldc, st);
+    return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "SIMT GEMM launch");
+  }
+  rc = run_tc(a, c.tc, A, B, true, la, lb, ldc, st);
+  if (scratch) cudaFreeAsync(scratch, st);
+  return rc;
+}
+
+int tforge_matmul(const float *A, const float *B, float *out, int64_t M, int64_t N, int64_t K,
+                  int mode, void *stream) {
+  tforge_gemm_args a{TFORGE_MATMUL, mode, TFORGE_F32, TFORGE_F32, A, B, nullptr, nullptr, out, M, N, K, 0, 0, 0};
+  return tforge_gemm(&a, stream);
+}
+
+int tforge_mbr(const float *A, const float *B, const float *bias, float *out, int64_t M, int64_t N,
+               int64_t K, int mode, void *stream) {
+  tforge_gemm_args a{TFORGE_MBR, mode, TFORGE_F32, TFORGE_F32, A, B, bias, nullptr, out, M, N, K, 0, 0, 0};
+  return tforge_gemm(&a, stream);
+}
+
+int tforge_matmul_add(const float *A, const float *B, const float *C_res, float *out, int64_t M,
+                      int64_t N, int64_t K, int mode, void *stream) {
+  tforge_gemm_args a{TFORGE_MATMUL_ADD, mode, TFORGE_F32, TFORGE_F32, A, B, nullptr, C_res, out, M, N, K, 0, 0, 0};
+  return tforge_gemm(&a, stream);
+}
+
+static int elementwise(int op, const float *X, const float *Y, float *Z, int64_t M, int64_t N,
+                       void *stream) {
+  if (M < 0 || N < 0) return TFORGE_ERR_SHAPE;
+  if (M == 0 || N == 0) return TFORGE_OK;
+  if (!X || !Z || (op != 1 && !Y)) return TFORGE_ERR_NULL;
+  if (!aligned(X, 4) || !aligned(Z, 4) || !aligned(Y, 4)) return TFORGE_ERR_ALIGN;
+  const size_t zb = (size_t)M * N * 4;
+  if (overlaps(Z, zb, X, zb) || (op == 0 && overlaps(Z, zb, Y, zb)) ||
+      (op == 2 && overlaps(Z, zb, Y, (size_t)N * 4)))
+    return TFORGE_ERR_ALIAS;
+  cudaError_t e = launch_elementwise(op, X, Y, Z, M, N, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "elementwise launch");
+}
+
+int tforge_bias_add(const float *X, const float *bias, float *Y, int64_t M, int64_t N, void *stream) {
+  return elementwise(2, X, bias, Y, M, N, stream);
+}
+int tforge_relu(const float *X, float *Y, int64_t M, int64_t N, void *stream) {
+  return elementwise(1, X, nullptr, Y, M, N, stream);
+}
+int tforge_add(const float *X, const float *Y, float *Z, int64_t M, int64_t N, void *stream) {
+  return elementwise(0, X, Y, Z, M, N, stream);
+}
+
+int tforge_convert_bf16(const float *x, uint16_t *y, int64_t n, void *stream) {
+  if (n < 0) return TFORGE_ERR_SHAPE;
+  if (n == 0) return TFORGE_OK;
+  if (!x || !y) return TFORGE_ERR_NULL;
+  if (!aligned(x, 4) || !aligned(y, 2)) return TFORGE_ERR_ALIGN;
+  if (overlaps(x, (size_t)n * 4, y, (size_t)n * 2)) return TFORGE_ERR_ALIAS;
+  cudaError_t e = launch_convert_bf16(x, y, n, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "bf16 conversion");
+}
+
+int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tforge_launch *out) {
+  if (!out) return TFORGE_ERR_NULL;
+  if (M < 0 || N < 0 || K < 0) return TFORGE_ERR_SHAPE;
+  if (mode < TFORGE_MODE_FP32 || mode > TFORGE_MODE_FP32_EXACT) return TFORGE_ERR_MODE;
+  std::memset(out, 0, sizeof(*out));
+  out->cluster[0] = out->cluster[1] = out->cluster[2] = 1;
+  out->mode = mode;
+  out->split_k = 1;
+  out->regs = out->static_smem = out->blocks_per_sm = -1;
+  const int epi = workload == TFORGE_MBR ? EPI_MBR : (workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
+  int ndev = 0;
+  const bool have_dev = cudaGetDeviceCount(&ndev) == cudaSuccess && ndev > 0;
+  auto fill_attrs = [&](cudaError_t e, const cudaFuncAttributes &fa, int blocks) {
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return;
+    }
+    out->regs = fa.numRegs;
+    out->static_smem = (int)fa.sharedSizeBytes;
+    out->blocks_per_sm = blocks;
+  };
+  if (workload >= TFORGE_BIAS_ADD && workload <= TFORGE_ADD) {
+    std::snprintf(out->kernel, sizeof(out->kernel), "tf_elementwise");
+    out->block[0] = 256;
+    out->block[1] = out->block[2] = 1;
+    const int64_t n4 = (M * N + 3) / 4;
+    int64_t g = (n4 + 255) / 256;
+    out->grid[0] = (int)(g > 148 * 16 ? 148 * 16 : (g < 1 ? 1 : g));
+    out->grid[1] = out->grid[2] = 1;
+    return TFORGE_OK;
+  }
+  if (workload < TFORGE_MATMUL || workload > TFORGE_MATMUL_ADD) return TFORGE_ERR_MODE;
+  const bool tma_ok = (K % 4 == 0) && (N % 4 == 0) && (mode != TFORGE_MODE_BF16 || (K % 8 == 0 && N % 8 == 0));
+  const Choice c = choose(mode, M, N, K, tma_ok);
+  if (c.kind < 0) return TFORGE_ERR_UNSUPPORTED;
+  if (c.kind == K_SIMT) {
+    std::snprintf(out->kernel, sizeof(out->kernel), "tf_gemm_simt_ffma");
+    int smem = 0;
+    simt_launch_shape(M, N, out->grid, out->block, &smem);
+    out->smem_bytes = smem;
+    out->tile[0] = 128;
+    out->tile[1] = 128;
+    out->tile[2] = 8;
+    out->stages = 2;
+    out->mode = TFORGE_MODE_FP32_EXACT;
+    if (have_dev) {
+      cudaFuncAttributes fa{};
+      int blocks = 0;
+      cudaError_t e = simt_func_attributes(epi, &fa, &blocks);
+      fill_attrs(e, fa, blocks);
+    }
+    return TFORGE_OK;
+  }
+  static const char *names[3] = {"tf_gemm_tcgen05_tf32", "tf_gemm_tcgen05_3xtf32", "tf_gemm_tcgen05_bf16"};
+  std::snprintf(out->kernel, sizeof(out->kernel), "%s", names[c.tc.prec]);
+  out->grid[0] = (int)((N + c.tc.bn - 1) / c.tc.bn);
+  out->grid[1] = (int)((M + 127) / 128);
+  out->grid[2] = 1;
+  out->block[0] = 256;
+  out->block[1] = out->block[2] = 1;
+  out->smem_bytes = tc_smem_bytes(c.tc);
+  out->tile[0] = 128;
+  out->tile[1] = c.tc.bn;
+  out->tile[2] = c.tc.prec == PREC_BF16 ? 64 : 32;
+  out->stages = c.tc.stages;
+  out->tmem_cols = c.tc.bn;
+  if (have_dev) {
+    cudaFuncAttributes fa{};
+    int blocks = 0;
+    cudaError_t e = tc_func_attributes(c.tc, epi, &fa, &blocks);
+    fill_attrs(e, fa, blocks);
+  }
+  return TFORGE_OK;
+}
+
+int tforge_set_config(const tforge_config *cfg) {
+  std::lock_guard<std::mutex> lk(g_cfg_mu);
+  if (!cfg) {
+    g_cfg = tforge_config{};
+    return TFORGE_OK;
+  }
+  if (cfg->kernel < 0 || cfg->kernel > 2) return TFORGE_ERR_MODE;
+  g_cfg = *cfg;
+  return TFORGE_OK;
+}
+
+int tforge_device_status(void *stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t *w = nullptr;
+  int rc = status_word(&w);
+  if (rc) return rc;
+  uint32_t v = 0;
+  e = cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  if (v) {
+    e = cudaMemset(w, 0, 4);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+  }
+  return (int)v;
+}
+
+int tforge_set_wait_limit_ns(uint64_t ns) {
+  g_wait_limit_ns.store(ns ? ns : 1000000000ull);
+  return TFORGE_OK;
+}
+
+int tforge_debug_skip_load(int on) {
+  g_debug_skip.store(on ? 1 : 0);
+  return TFORGE_OK;
+}
+
+const char *tforge_status_string(int s) {
+  switch (s) {
+    case TFORGE_OK: return "ok";
+    case TFORGE_ERR_SHAPE: return "invalid shape or pitch";
+    case TFORGE_ERR_ALIGN: return "misaligned pointer";
+    case TFORGE_ERR_ALIAS: return "output overlaps an input";
+    case TFORGE_ERR_MODE: return "unknown mode, workload or dtype";
+    case TFORGE_ERR_CUDA: return "CUDA error";
+    case TFORGE_ERR_TIMEOUT: return "device-side wait timed out";
+    case TFORGE_ERR_NULL: return "null pointer";
+    case TFORGE_ERR_UNSUPPORTED: return "unsupported configuration";
+    case TFORGE_ERR_NOMEM: return "out of memory";
+  }
+  return "unknown status";
+}
+
+const char *tforge_last_error(void) { return g_last_error.c_str(); }
+const char *tforge_version(void) { return "tforge-b200 0.1 (sm_100a)"; }
+
+int tforge_malloc(void **ptr, uint64_t bytes) {
+  if (!ptr) return TFORGE_ERR_NULL;
+  cudaError_t e = cudaMalloc(ptr, bytes ? bytes : 1);
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaMalloc");
+}
+int tforge_free(void *ptr) {
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaFree");
+}
+int tforge_memcpy_h2d(void *dst, const void *src, uint64_t bytes, void *stream) {
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaMemcpyAsync(H2D)");
+}
+int tforge_memcpy_d2h(void *dst, const void *src, uint64_t bytes, void *stream) {
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaMemcpyAsync(D2H)");
+}
+int tforge_memset(void *dst, int byte, uint64_t bytes, void *stream) {
+  cudaError_t e = cudaMemsetAsync(dst, byte, bytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaMemsetAsync");
+}
+int tforge_stream_sync(void *stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaStreamSynchronize");
+}
+int tforge_device_count(int *n) {
+  if (!n) return TFORGE_ERR_NULL;
+  cudaError_t e = cudaGetDeviceCount(n);
+  if (e != cudaSuccess) {
+    *n = 0;
+    return cuda_fail(e, "cudaGetDeviceCount");
+  }
+  return TFORGE_OK;
+}
+int tforge_set_device(int dev) {
+  cudaError_t e = cudaSetDevice(dev);
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaSetDevice");
+}
+
+}  // extern "C"

@@ -1,0 +1,323 @@
+// tf_gemm_tc.cu -- fused GEMM on the sm_100a tensor cores (tcgen05 + TMA + TMEM).
+//
+// Computes out = epilogue(A @ B) for the tforge ops matmul, mbr = relu(A @ B + bias)
+// and matmul_add = A @ B + C_res (include/TensorForge/Dialect/TForge/TForgeOps.td:37-113).
+// It replaces the staged SIMT kernel that lib/Transforms/Gpu.cpp:219-316 generates
+// (BM x BN block tiles, a K loop over shared-memory tiles, the epilogue fused in
+// registers) with a Blackwell pipeline:
+//
+//   warp 0      TMA producer: one thread loads the A tile (BM x BK, K-major, 128-byte
+//               swizzle) and the B tile (BK x BN, N-contiguous "MN-major", 128-byte
+//               swizzle) of each stage into a STAGES-deep shared-memory ring.
+//   warps 2..7  (3xTF32 only) converters: split each landed f32 tile in place into
+//               hi = tf32(x) and lo = tf32(x - hi) in a second buffer.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN) into a TMEM
+//               accumulator; tcgen05.commit frees each stage and finally signals the
+//               epilogue.  3xTF32 issues lo*hi, hi*lo, hi*hi per K step.
+//   warps 4..7  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//               32(w%4)..+31 = its 32 output rows), + bias / + C_res, IEEE maximum
+//               with +0.0, 16-byte vector stores.  No M x N temporary exists.
+//
+// Edge tiles need no padding copies (the reference pads inside the timed region,
+// runners/gpu/tforge-gpu-bench.cu:293-301): TMA fills out-of-range elements with
+// zeros and the epilogue predicates its stores.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "tf_internal.h"
+#include "tf_ptx.cuh"
+
+namespace tf {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 256;
+constexpr int kConvThreads = 192;  // warps 2..7
+
+template <int PREC, int BN, int STAGES>
+struct TcLayout {
+  static constexpr int kElem = PREC == PREC_BF16 ? 2 : 4;
+  static constexpr int kBK = 128 / kElem;             // K elements per stage (one 128-B row)
+  static constexpr int kUmmaK = 32 / kElem;           // K per MMA instruction (32 bytes)
+  static constexpr int kKSteps = kBK / kUmmaK;        // 4
+  static constexpr int kNBlk = 128 / kElem;           // N elements per 128-B MN block
+  static constexpr int kBBlocks = BN / kNBlk;         // TMA boxes per B stage
+  // MN-major B descriptor: swizzle mode and the byte stride between K row groups.
+  static constexpr uint32_t kBSwz = kElem == 4 ? 1u : 2u;
+  static constexpr uint32_t kBSbo = kElem == 4 ? 512u : 1024u;
+  static constexpr int kABytes = kBM * 128;           // 16 KB
+  static constexpr int kBBytes = BN * kElem * kBK;    // BN * 128
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kLoBytes = PREC == PREC_X3 ? kStageBytes : 0;
+  static constexpr int kRingBytes = STAGES * (kStageBytes + kLoBytes);
+  static constexpr int kBarBytes = 8 * (3 * STAGES + 1) + 16;
+  static constexpr int kSmemBytes = 1024 + kRingBytes + kBarBytes;
+  // Shared-memory offsets (relative to the 1024-aligned base).
+  static constexpr int a_off(int s) { return s * kStageBytes; }
+  static constexpr int b_off(int s) { return s * kStageBytes + kABytes; }
+  static constexpr int lo_off(int s) { return STAGES * kStageBytes + s * kLoBytes; }
+  static constexpr int bar_off() { return kRingBytes; }
+};
+
+template <int PREC, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcParams p) {
+  using L = TcLayout<PREC, BN, STAGES>;
+  constexpr bool kTF32 = PREC != PREC_BF16;
+  constexpr uint32_t kIdesc = instr_desc(kTF32 ? 2u : 1u, kBM, BN);
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off());
+  // full[s]: TMA landed; conv[s]: hi/lo split done (3xTF32); empty[s]: MMAs done; accf.
+  const uint32_t full0 = smem_u32(bars), conv0 = full0 + 8 * STAGES, empty0 = conv0 + 8 * STAGES,
+                 accf = empty0 + 8 * STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 1);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+  const int nkb = (p.K + L::kBK - 1) / L::kBK;
+  const WaitCtl wc{abort_flag, p.status, p.limit_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(conv0 + 8 * s, kConvThreads);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(accf, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_acc = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int kb = 0;
+    for (; kb < nkb; ++kb) {
+      const int s = kb % STAGES, round = kb / STAGES;
+      if (round > 0 && !mbar_wait(empty0 + 8 * s, (round - 1) & 1, wc)) break;
+      if (p.debug_skip && kb == 0) continue;  // test hook: this stage never fills
+      mbar_arrive_expect_tx(full0 + 8 * s, L::kStageBytes);
+      const int kc = kb * L::kBK;
+      tma_load_2d(sbase + L::a_off(s), &tmA, kc, m0, full0 + 8 * s);
+#pragma unroll
+      for (int j = 0; j < L::kBBlocks; ++j)
+        tma_load_2d(sbase + L::b_off(s) + j * (L::kBK * 128), &tmB, n0 + j * L::kNBlk, kc,
+                    full0 + 8 * s);
+    }
+    if (*abort_flag) {
+      // Drain: wait (bounded) for the last load issued into each stage before the CTA
+      // exits.  Loads kb' < kb were issued (except a skipped kb' = 0).
+#pragma unroll 1
+      for (int s = 0; s < STAGES; ++s) {
+        if (kb - 1 < s) continue;
+        const int last = kb - 1 - ((kb - 1 - s) % STAGES);
+        if (p.debug_skip && last == 0) continue;
+        mbar_wait_drain(full0 + 8 * s, (last / STAGES) & 1, p.limit_ns);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t ready0 = PREC == PREC_X3 ? conv0 : full0;
+    uint32_t accum = 0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % STAGES, round = kb / STAGES;
+      if (!mbar_wait(ready0 + 8 * s, round & 1, wc)) break;
+      tc_fence_after();
+      const uint32_t a_hi = sbase + L::a_off(s), b_hi = sbase + L::b_off(s);
+#pragma unroll
+      for (int ks = 0; ks < L::kKSteps; ++ks) {
+        // A: K-major, 128-B swizzle, 8-row core groups 1024 B apart; a K step is 32 B
+        //    along the row.
+        // B: MN-major, 128-B MN blocks kBK*128 B apart.  16-bit elements use the 128-B
+        //    swizzle (16-B atoms, K groups of 8 rows = 1024 B); 32-bit elements must use
+        //    the 128-B swizzle with 32-B atoms (layout type 1, K groups of 4 rows = 512 B),
+        //    which the B tensor map writes (CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+        const uint64_t ad = smem_desc(a_hi + ks * 32, 16, 1024, 2);
+        const uint64_t bd = smem_desc(b_hi + ks * L::kUmmaK * 128, L::kBK * 128, L::kBSbo, L::kBSwz);
+        if constexpr (PREC == PREC_X3) {
+          const uint32_t lo = sbase + L::lo_off(s);
+          const uint64_t ad_lo = smem_desc(lo + ks * 32, 16, 1024, 2);
+          const uint64_t bd_lo = smem_desc(lo + L::kABytes + ks * L::kUmmaK * 128, L::kBK * 128,
+                                           L::kBSbo, L::kBSwz);
+          mma_ss<true>(tmem_acc, ad_lo, bd, kIdesc, accum);
+          mma_ss<true>(tmem_acc, ad, bd_lo, kIdesc, 1u);
+          mma_ss<true>(tmem_acc, ad, bd, kIdesc, 1u);
+        } else {
+          mma_ss<kTF32>(tmem_acc, ad, bd, kIdesc, accum);
+        }
+        accum = 1u;
+      }
+      mma_commit(empty0 + 8 * s);
+    }
+    mma_commit(accf);
+    if (*abort_flag) mbar_wait_drain(accf, 0, p.limit_ns);  // MMAs done before TMEM is freed
+  } else if (PREC == PREC_X3 && warp >= 2) {
+    // ---------------- 3xTF32 converters ----------------
+    const int t = threadIdx.x - 64;
+    constexpr int kChunks = L::kStageBytes / 16;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % STAGES, round = kb / STAGES;
+      if (!mbar_wait(full0 + 8 * s, round & 1, wc)) break;
+      float4 *raw = reinterpret_cast<float4 *>(smem + L::a_off(s));
+      float4 *lo = reinterpret_cast<float4 *>(smem + L::lo_off(s));
+#pragma unroll 4
+      for (int c = t; c < kChunks; c += kConvThreads) {
+        float4 x = raw[c], h, l;
+        h.x = to_tf32(x.x); h.y = to_tf32(x.y); h.z = to_tf32(x.z); h.w = to_tf32(x.w);
+        l.x = isfinite(h.x) ? to_tf32(x.x - h.x) : 0.f;
+        l.y = isfinite(h.y) ? to_tf32(x.y - h.y) : 0.f;
+        l.z = isfinite(h.z) ? to_tf32(x.z - h.z) : 0.f;
+        l.w = isfinite(h.w) ? to_tf32(x.w - h.w) : 0.f;
+        raw[c] = h;
+        lo[c] = l;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(conv0 + 8 * s);
+    }
+  }
+
+  // ---------------- epilogue: TMEM -> registers -> global ----------------
+  if (warp >= 4) {
+    if (mbar_wait(accf, 0, wc)) {
+      tc_fence_after();
+      const int q = warp & 3;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      float *orow = p.out + (int64_t)row * p.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_acc + ((uint32_t)(q * 32) << 16) + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const int col = col0 + j;
+            if (col < p.N) {
+              float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                     __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+              if constexpr (EPI == EPI_MBR) {
+                const float4 b = __ldg(reinterpret_cast<const float4 *>(p.bias + col));
+                v.x = relu_ieee(__fadd_rn(v.x, b.x));
+                v.y = relu_ieee(__fadd_rn(v.y, b.y));
+                v.z = relu_ieee(__fadd_rn(v.z, b.z));
+                v.w = relu_ieee(__fadd_rn(v.w, b.w));
+              } else if constexpr (EPI == EPI_ADD) {
+                const float4 cr = __ldg(reinterpret_cast<const float4 *>(
+                    p.cres + (int64_t)row * p.ldc + col));
+                v.x = __fadd_rn(v.x, cr.x);
+                v.y = __fadd_rn(v.y, cr.y);
+                v.z = __fadd_rn(v.z, cr.z);
+                v.w = __fadd_rn(v.w, cr.w);
+              }
+              *reinterpret_cast<float4 *>(orow + col) = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_acc, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+template <int PREC, int BN, int STAGES, int EPI>
+static cudaError_t launch_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
+                              cudaStream_t stream) {
+  using L = TcLayout<PREC, BN, STAGES>;
+  auto kern = gemm_tc_kernel<PREC, BN, STAGES, EPI>;
+  // The shared-memory opt-in is per device: remember which devices have it.
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
+  }
+  dim3 grid((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM, 1);
+  kern<<<grid, kThreads, L::kSmemBytes, stream>>>(tmA, tmB, p);
+  return cudaGetLastError();
+}
+
+template <int PREC, int BN, int STAGES>
+static cudaError_t launch_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &tmB,
+                              const TcParams &p, cudaStream_t stream) {
+  switch (epi) {
+    case EPI_MATMUL: return launch_one<PREC, BN, STAGES, EPI_MATMUL>(tmA, tmB, p, stream);
+    case EPI_MBR: return launch_one<PREC, BN, STAGES, EPI_MBR>(tmA, tmB, p, stream);
+    case EPI_ADD: return launch_one<PREC, BN, STAGES, EPI_ADD>(tmA, tmB, p, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// The instantiated (precision, BN, stages) set; the dispatch table picks among these.
+#define TF_TC_CONFIGS(X)                                                           \
+  X(PREC_TF32, 256, 4) X(PREC_TF32, 128, 6) X(PREC_TF32, 64, 8)                    \
+  X(PREC_BF16, 256, 4) X(PREC_BF16, 128, 6) X(PREC_BF16, 64, 8)                    \
+  X(PREC_X3, 256, 2) X(PREC_X3, 128, 3) X(PREC_X3, 64, 4)
+
+int tc_smem_bytes(const TcConfig &c) {
+#define TF_SMEM(P, B, S) \
+  if (c.prec == P && c.bn == B && c.stages == S) return TcLayout<P, B, S>::kSmemBytes;
+  TF_TC_CONFIGS(TF_SMEM)
+#undef TF_SMEM
+  return -1;
+}
+
+bool tc_config_supported(const TcConfig &c) { return tc_smem_bytes(c) > 0; }
+
+template <int P, int B, int S>
+static cudaError_t attrs_epi(int epi, cudaFuncAttributes *a, int *blocks) {
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_tc_kernel<P, B, S, EPI_MBR>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_tc_kernel<P, B, S, EPI_ADD>)
+                                   : reinterpret_cast<const void *>(gemm_tc_kernel<P, B, S, EPI_MATMUL>);
+  cudaError_t e = cudaFuncGetAttributes(a, f);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<P, B, S>::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, f, kThreads, TcLayout<P, B, S>::kSmemBytes);
+}
+
+cudaError_t tc_func_attributes(const TcConfig &c, int epi, cudaFuncAttributes *a, int *blocks) {
+#define TF_ATTR(P, B, S) \
+  if (c.prec == P && c.bn == B && c.stages == S) return attrs_epi<P, B, S>(epi, a, blocks);
+  TF_TC_CONFIGS(TF_ATTR)
+#undef TF_ATTR
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm_tc(const TcConfig &c, int epi, const CUtensorMap &tmA,
+                           const CUtensorMap &tmB, const TcParams &p, cudaStream_t stream) {
+#define TF_LAUNCH(P, B, S) \
+  if (c.prec == P && c.bn == B && c.stages == S) return launch_epi<P, B, S>(epi, tmA, tmB, p, stream);
+  TF_TC_CONFIGS(TF_LAUNCH)
+#undef TF_LAUNCH
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace tf

@@ -1,0 +1,57 @@
+// tf_internal.h -- declarations shared by the library's translation units (not public).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace tf {
+
+enum Epi : int { EPI_MATMUL = 0, EPI_MBR = 1, EPI_ADD = 2 };
+// Tensor-core precision paths: one TF32 product, the 3xTF32 split, or bf16 operands.
+enum Prec : int { PREC_TF32 = 0, PREC_X3 = 1, PREC_BF16 = 2 };
+
+// Parameters of the tcgen05 kernel besides the two tensor maps.
+struct TcParams {
+  const float *bias;   // N (mbr)
+  const float *cres;   // M x N, pitch ldc (matmul_add)
+  float *out;          // M x N, pitch ldc
+  int32_t M, N, K;
+  int64_t ldc;
+  uint32_t *status;    // device status word
+  uint64_t limit_ns;   // bounded-wait limit
+  int32_t debug_skip;  // test hook: skip the first stage's loads
+};
+
+struct TcConfig {
+  int prec;    // Prec
+  int bn;      // 64, 128, 256
+  int stages;
+};
+
+// Dynamic shared memory the tcgen05 kernel needs for a configuration.
+int tc_smem_bytes(const TcConfig &cfg);
+// True when a kernel instantiation exists for the configuration.
+bool tc_config_supported(const TcConfig &cfg);
+// Launches the tcgen05 kernel.  tmA / tmB are encoded by the caller.
+cudaError_t launch_gemm_tc(const TcConfig &cfg, int epi, const CUtensorMap &tmA,
+                           const CUtensorMap &tmB, const TcParams &p, cudaStream_t stream);
+
+// Registers / static shared memory of an instantiation and resident CTAs per SM
+// (needs a device).
+cudaError_t tc_func_attributes(const TcConfig &cfg, int epi, cudaFuncAttributes *attr,
+                               int *blocks_per_sm);
+cudaError_t simt_func_attributes(int epi, cudaFuncAttributes *attr, int *blocks_per_sm);
+
+// SIMT sequential-k FFMA GEMM (bitwise equal to the reference's generated kernels).
+cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const float *aux, float *C,
+                             int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                             int64_t ldc, cudaStream_t stream);
+void simt_launch_shape(int64_t M, int64_t N, int grid[3], int block[3], int *smem);
+
+// Elementwise ops: op 0 add, 1 relu, 2 bias_add.
+cudaError_t launch_elementwise(int op, const float *X, const float *Y, float *Z, int64_t M,
+                               int64_t N, cudaStream_t stream);
+cudaError_t launch_convert_bf16(const float *x, uint16_t *y, int64_t n, cudaStream_t stream);
+
+}  // namespace tf

@@ -1,0 +1,132 @@
+"""The C-ABI library loads, exports every declared symbol, and validates arguments
+without a GPU (no compute calls here)."""
+
+import ctypes as C
+import pathlib
+import re
+
+import pytest
+
+from tensorforge_b200 import _lib, tforge_gpu as tg
+
+REPO = pathlib.Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    text = "\n".join(p.read_text() for p in (REPO / "include").glob("*.h"))
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tforge_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    for s in syms:
+        assert hasattr(L, s), s
+    # and the ctypes signature table covers them all
+    assert set(syms) <= set(_lib.SIGNATURES), set(syms) - set(_lib.SIGNATURES)
+
+
+def test_version_and_status_strings():
+    L = _lib.lib()
+    assert b"sm_100a" in L.tforge_version()
+    for code in range(10):
+        assert L.tforge_status_string(code)
+    assert L.tforge_status_string(_lib.ERR_TIMEOUT) == b"device-side wait timed out"
+
+
+P = 1 << 20  # fake, 16-byte aligned "device" addresses: validation happens before any CUDA call
+
+
+@pytest.mark.parametrize("call,code", [
+    (lambda L: L.tforge_mbr(None, None, None, None, 4, 4, 4, 0, None), _lib.ERR_NULL),
+    (lambda L: L.tforge_mbr(P, 2 * P, 3 * P, 4 * P, -1, 4, 4, 0, None), _lib.ERR_SHAPE),
+    (lambda L: L.tforge_mbr(P, 2 * P, 3 * P, 4 * P, 4, 4, 4, 9, None), _lib.ERR_MODE),
+    (lambda L: L.tforge_mbr(P + 2, 2 * P, 3 * P, 4 * P, 4, 4, 4, 0, None), _lib.ERR_ALIGN),
+    (lambda L: L.tforge_mbr(P, 2 * P, 3 * P, P + 16, 8, 8, 8, 0, None), _lib.ERR_ALIAS),
+    (lambda L: L.tforge_matmul_add(P, 2 * P, 4 * P + 8, 4 * P, 8, 8, 8, 0, None), _lib.ERR_ALIAS),
+    (lambda L: L.tforge_matmul(P, None, 4 * P, 8, 8, 8, 0, None), _lib.ERR_NULL),
+    (lambda L: L.tforge_relu(P, P, 4, 4, None), _lib.ERR_ALIAS),
+    (lambda L: L.tforge_add(P, 2 * P, 3 * P, -2, 4, None), _lib.ERR_SHAPE),
+    (lambda L: L.tforge_bias_add(P, None, 3 * P, 2, 4, None), _lib.ERR_NULL),
+    (lambda L: L.tforge_convert_bf16(P, P + 2, 16, None), _lib.ERR_ALIAS),
+])
+def test_argument_validation(call, code):
+    assert call(_lib.lib()) == code
+
+
+def test_empty_problems_are_noops():
+    L = _lib.lib()
+    assert L.tforge_mbr(None, None, None, None, 0, 16, 16, 0, None) == 0
+    assert L.tforge_matmul(None, None, None, 16, 0, 16, 0, None) == 0
+    assert L.tforge_relu(None, None, 0, 0, None) == 0
+
+
+def test_bf16_operands_need_bf16_mode():
+    args = _lib.GemmArgs(0, 0, _lib.BF16, _lib.F32, P, 2 * P, None, None, 4 * P, 8, 8, 8, 0, 0, 0)
+    assert _lib.lib().tforge_gemm(C.byref(args), None) == _lib.ERR_MODE
+
+
+def test_pitch_smaller_than_row_is_rejected():
+    args = _lib.GemmArgs(0, 0, _lib.F32, _lib.F32, P, 2 * P, None, None, 4 * P, 8, 8, 8, 4, 0, 0)
+    assert _lib.lib().tforge_gemm(C.byref(args), None) == _lib.ERR_SHAPE
+
+
+@pytest.mark.parametrize("shape,mode,kernel", [
+    ((2048, 2048, 2048), "fp32", "tf_gemm_tcgen05_3xtf32"),
+    ((2048, 2048, 2048), "tf32", "tf_gemm_tcgen05_tf32"),
+    ((2048, 2048, 2048), "bf16", "tf_gemm_tcgen05_bf16"),
+    ((2048, 2048, 2048), "fp32_exact", "tf_gemm_simt_ffma"),
+    ((777, 1111, 333), "fp32", "tf_gemm_simt_ffma"),   # pitches not 16-byte multiples
+    ((256, 256, 8), "fp32", "tf_gemm_simt_ffma"),      # K < 16: exact kernel keeps the fp32 bound
+    ((256, 256, 0), "tf32", "tf_gemm_simt_ffma"),      # K = 0: out = epilogue(+0)
+])
+def test_dispatch_table(shape, mode, kernel):
+    d = _lib.describe("mbr", *shape, mode)
+    assert d["kernel"] == kernel
+    assert d["block"] == [256, 1, 1]
+    if kernel.startswith("tf_gemm_tcgen05"):
+        m, n, _ = shape
+        assert d["grid"] == [-(-n // d["tile"][1]), -(-m // 128), 1]
+        assert d["smem_bytes"] <= 232448
+        assert d["tmem_cols"] == d["tile"][1]
+
+
+def test_forced_config_and_reset():
+    _lib.set_config(1, 128, 6)
+    try:
+        d = _lib.describe("mbr", 2048, 2048, 2048, "tf32")
+        assert d["tile"][1] == 128 and d["stages"] == 6
+        _lib.set_config(1, 96, 6)  # not instantiated
+        with pytest.raises(_lib.TforgeError):
+            _lib.describe("mbr", 2048, 2048, 2048, "tf32")
+    finally:
+        _lib.set_config()
+    assert _lib.describe("mbr", 2048, 2048, 2048, "tf32")["tile"][1] == 256
+
+
+def test_compile_kernel_writes_launch_json(tmp_path, monkeypatch):
+    monkeypatch.setattr(tg, "ART", tmp_path)
+    d, launch = tg.compile_kernel("mbr", 512, 512, 512, "precision=tf32 bn=128 stages=6", tag="t")
+    assert tg.parse_launch(d / "launch.json") == launch
+    for key in ("kernel", "grid", "block", "args", "padded"):  # the reference's launch.json keys
+        assert key in launch
+    assert launch["args"] == ["arg0", "arg1", "arg2", "arg3"]
+    assert launch["padded"] == [512, 512, 512]
+    assert launch["tile"] == [128, 128, 32]
+    assert tg.padded_shape(777, 1111, 333, "") == (777, 1111, 333)
+
+
+def test_ptxas_resources_reports_no_spills():
+    res = tg.ptxas_resources(launch={"kernel": "tf_gemm_tcgen05_3xtf32"})
+    assert res["regs"] > 0
+    assert res["spill_stores"] == 0 and res["spill_loads"] == 0
+
+
+def test_tensor_roofline_from_measured_peaks():
+    peaks = {"bf16_tflops": 1600.0}
+    assert tg.tensor_roofline_tflops("bf16", peaks) == (1600.0, "of measured")
+    assert tg.tensor_roofline_tflops("tf32", peaks)[0] == 800.0
+    assert tg.tensor_roofline_tflops("fp32", peaks)[0] == pytest.approx(800.0 / 3)
+    assert tg.tensor_roofline_tflops("fp32", {})[1] == "of fallback"

@@ -1,0 +1,201 @@
+"""GPU parity: every kernel through the C-ABI against the CPU restatement and the
+reference's FP64 check.
+
+* fp32_exact (SIMT FFMA, sequential k): bit-exact against the restatement, i.e. the
+  reference's generated kernels (docs/numerics.md:3,53).
+* fp32 (3xTF32 on tcgen05): err/bound <= 1 with the reference's bound
+  gamma_{K+1}(|A||B| + |bias|) (python/tforge_cpu.py:128-145).
+* tf32 / bf16: err/bound <= 1 against the stated looser bound that adds the input
+  rounding term (2u + u^2)|A||B|, u = 2^-10 (TF32 truncation) or 2^-8 (bf16).
+* elementwise ops: bit-exact.
+"""
+
+import ctypes as C
+import json
+import subprocess
+
+import numpy as np
+import pytest
+
+from tensorforge_b200 import _lib, tforge_cpu as tc, tforge_gpu as tg
+
+pytestmark = pytest.mark.gpu
+
+EXACT_SHAPES = [(256, 256, 128), (777, 1111, 333), (1000, 1000, 1000), (7, 19, 5), (1, 1, 1),
+                (130, 260, 36), (256, 256, 0)]
+TC_SHAPES = [(256, 256, 128), (2048, 2048, 2048), (1000, 1000, 1000), (512, 512, 4096), (129, 264, 36),
+             (300, 8, 64), (4, 2048, 128), (1, 4, 16), (513, 1000, 520), (128, 256, 2048)]
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+@pytest.mark.parametrize("shape", EXACT_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("workload", ["matmul", "mbr", "matmul_add"])
+def test_fp32_exact_is_bitwise_reference(gpu, oracle, workload, shape):
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 1234)
+    out = tg.run_op(workload, ins, m, n, k, "fp32_exact")
+    ref = oracle.gemm(workload, ins)
+    assert np.array_equal(bits(out), bits(ref))
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
+@pytest.mark.parametrize("workload", ["mbr", "matmul", "matmul_add"])
+def test_tensor_core_modes_within_bound(gpu, workload, mode, shape):
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 1234)
+    out = tg.run_op(workload, ins, m, n, k, mode)
+    res = tc.check_output(workload, ins, out, mode)
+    assert res["nan_count"] == 0
+    assert res["err_over_bound"] <= 1.0, res
+
+
+@pytest.mark.parametrize("seed", [0, 1234])
+def test_config1_fp32_mode(gpu, seed):
+    """relu(x @ w + b), x 256x128, w 128x256, seeds 0 and 1234."""
+    ins = tc.make_inputs("mbr", 256, 256, 128, seed)
+    d = _lib.describe("mbr", 256, 256, 128, "fp32")
+    assert d["kernel"] == "tf_gemm_tcgen05_3xtf32"
+    out = tg.run_op("mbr", ins, 256, 256, 128, "fp32")
+    res = tc.check_output("mbr", ins, out)
+    assert res["pass"] and res["err_over_bound"] < 0.25, res
+
+
+@pytest.mark.parametrize("bn,stages", [(256, 2), (128, 3), (64, 4)])
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
+def test_every_instantiated_config(gpu, mode, bn, stages):
+    st = {"fp32": stages, "tf32": {256: 4, 128: 6, 64: 8}[bn], "bf16": {256: 4, 128: 6, 64: 8}[bn]}[mode]
+    m, n, k = 384, 520, 200
+    ins = tc.make_inputs("mbr", m, n, k, 5)
+    out = tg.run_op("mbr", ins, m, n, k, mode, options=f"bn={bn} stages={st}")
+    res = tc.check_output("mbr", ins, out, mode)
+    assert res["pass"], res
+
+
+@pytest.mark.parametrize("shape", [(33, 17), (256, 1024), (1000, 999), (1, 1), (4096, 4096)])
+@pytest.mark.parametrize("workload", ["relu", "bias_add", "add"])
+def test_elementwise_bitwise(gpu, oracle, workload, shape):
+    m, n = shape
+    ins = tc.make_inputs(workload, m, n, None, 99)
+    if workload == "relu":
+        ins["a"].ravel()[:5] = np.array([-1.0, -0.0, np.nan, 2.5, 0.0], dtype=np.float32)[: ins["a"].size]
+    out = tg.run_op(workload, ins, m, n, None)
+    assert np.array_equal(bits(out), bits(oracle.elementwise(workload, ins)))
+    assert tc.check_elementwise(workload, ins, out)["pass"]
+
+
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16", "fp32_exact"])
+def test_epilogue_nan_and_signed_zero(gpu, mode):
+    """relu = IEEE maximum: NaN propagates, no -0.0 ever leaves the kernel."""
+    m, n, k = 256, 256, 64
+    ins = tc.make_inputs("mbr", m, n, k, 11)
+    ins["a"][3, 5] = np.nan
+    ins["bias"][:8] = -0.0
+    out = tg.run_op("mbr", ins, m, n, k, mode)
+    assert np.isnan(out[3]).all()
+    rest = np.delete(out, 3, axis=0)
+    assert not np.isnan(rest).any()
+    assert not (bits(rest) == 0x80000000).any()
+    assert (rest >= 0).all()
+
+
+def test_pitched_views(gpu):
+    """Sub-matrix views through lda/ldb/ldc (row shards and column blocks)."""
+    M, N, K, lda, ldb, ldc = 300, 200, 96, 128, 256, 256
+    rng = np.random.default_rng(3)
+    Abig = rng.uniform(-1, 1, (M, lda)).astype(np.float32)
+    Bbig = rng.uniform(-1, 1, (K, ldb)).astype(np.float32)
+    bias = rng.uniform(-1, 1, N).astype(np.float32)
+    a, b, bb = (tg.DeviceBuffer.upload(x) for x in (Abig, Bbig, bias))
+    out = tg.DeviceBuffer(M * ldc * 4)
+    try:
+        for mode in ("fp32", "tf32", "fp32_exact"):
+            _lib.check(_lib.lib().tforge_memset(out.ptr, 0, M * ldc * 4, None))
+            _lib.gemm("mbr", a.addr, b.addr, out.addr, M, N, K, mode, bias=bb.addr, lda=lda, ldb=ldb, ldc=ldc)
+            got = out.download((M, ldc))
+            ins = {"a": Abig[:, :K].copy(), "b": Bbig[:, :N].copy(), "bias": bias}
+            assert tc.check_output("mbr", ins, got[:, :N], mode)["pass"]
+            assert (got[:, N:] == 0).all()  # nothing written outside the view
+    finally:
+        for x in (a, b, bb, out):
+            x.free()
+
+
+def test_bf16_operands_match_f32_input_bf16_mode(gpu):
+    m, n, k = 512, 384, 256
+    ins = tc.make_inputs("mbr", m, n, k, 8)
+    ref = tg.run_op("mbr", ins, m, n, k, "bf16")
+    L = _lib.lib()
+    a, b, bias = (tg.DeviceBuffer.upload(ins[x]) for x in ("a", "b", "bias"))
+    a16, b16, out = tg.DeviceBuffer(m * k * 2), tg.DeviceBuffer(k * n * 2), tg.DeviceBuffer(m * n * 4)
+    try:
+        _lib.check(L.tforge_convert_bf16(a.ptr, a16.ptr, m * k, None))
+        _lib.check(L.tforge_convert_bf16(b.ptr, b16.ptr, k * n, None))
+        _lib.gemm("mbr", a16.addr, b16.addr, out.addr, m, n, k, "bf16", bias=bias.addr,
+                  a_dtype=_lib.BF16, b_dtype=_lib.BF16)
+        got = out.download((m, n))
+        assert np.array_equal(bits(got), bits(ref))
+    finally:
+        for x in (a, b, bias, a16, b16, out):
+            x.free()
+
+
+def test_large_square_row_subset(gpu):
+    """cfg3 8192^3 in fp32 mode: FP64 check on a seeded subset of 64 rows."""
+    m = n = k = 8192
+    ins = tc.make_inputs("mbr", m, n, k, 1234)
+    out = tg.run_op("mbr", ins, m, n, k, "fp32")
+    rows = np.sort(np.random.default_rng(0).choice(m, 64, replace=False))
+    res = tc.check_output("mbr", ins, out, "fp32", rows=rows)
+    assert res["pass"], res
+    assert not np.isnan(out).any()
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(gpu):
+    """A stage that never fills: the consumer's bounded wait expires, the kernel drains
+    and returns, the status word says TIMEOUT, and the next call is correct."""
+    L = _lib.lib()
+    m, n, k = 256, 256, 256
+    ins = tc.make_inputs("mbr", m, n, k, 2)
+    a, b, bias = (tg.DeviceBuffer.upload(ins[x]) for x in ("a", "b", "bias"))
+    out = tg.DeviceBuffer(m * n * 4)
+    try:
+        assert L.tforge_set_wait_limit_ns(50_000_000) == 0
+        assert L.tforge_debug_skip_load(1) == 0
+        _lib.gemm("mbr", a.addr, b.addr, out.addr, m, n, k, "tf32", bias=bias.addr)
+        assert _lib.device_status(None) == _lib.ERR_TIMEOUT
+    finally:
+        L.tforge_debug_skip_load(0)
+        L.tforge_set_wait_limit_ns(0)
+    _lib.gemm("mbr", a.addr, b.addr, out.addr, m, n, k, "tf32", bias=bias.addr)
+    assert _lib.device_status(None) == 0
+    assert tc.check_output("mbr", ins, out.download((m, n)), "tf32")["pass"]
+    for x in (a, b, bias, out):
+        x.free()
+
+
+def test_describe_reports_device_resources(gpu):
+    d = _lib.describe("mbr", 2048, 2048, 2048, "fp32")
+    assert d["regs"] > 0 and d["blocks_per_sm"] >= 1
+
+
+def test_runner_lib_and_cublas_modes(gpu, tmp_path):
+    for mode in ("lib", "cublas"):
+        r = json.loads(subprocess.run([str(tg.GPU_BENCH), "--mode", mode, "--workload", "mbr", "--m", "512",
+                                       "--n", "512", "--k", "512", "--warmup", "1", "--reps", "3"],
+                                      capture_output=True, text=True, check=True).stdout)
+        for key in ("gpu", "median_ms", "grid", "block", "sm_clock_median_mhz", "cuda_driver"):
+            assert key in r
+        assert r["median_ms"] > 0
+
+
+def test_shim_check_matches_reference_api(gpu):
+    """tg.check returns (res, out) like python/tforge_gpu.py:112-145, for lib and cuBLAS."""
+    for mode in ("kernel", "cublas"):
+        res, out = tg.check("mbr", 256, 256, 256, mode=mode)
+        assert res["pass"] and out.shape == (256, 256)
+    res, out = tg.check("relu", 64, 48, 1)
+    assert res["pass"]
