@@ -133,8 +133,8 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
 
 /* Force a kernel configuration (offline tuning sweeps); NULL restores the table. */
 typedef struct tforge_config {
-  int32_t kernel;        /* 0 = table, 1 = tcgen05 1-CTA, 2 = SIMT */
-  int32_t bn;            /* 64, 128 or 256 */
+  int32_t kernel;        /* 0 = table, 1 = tcgen05 one CTA per tile, 2 = SIMT, 3 = tcgen05 CTA pair */
+  int32_t bn;            /* 64, 128 or 256 (one-CTA kernel) */
   int32_t stages;
   int32_t persistent;
 } tforge_config;

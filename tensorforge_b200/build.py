@@ -23,7 +23,7 @@ BUILD = PKG / "_build"
 LIB = PKG / "libtforge_gpu.so"
 RUNNER = PKG / "tforge-gpu-bench"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-LIB_SOURCES = ["tf_api.cu", "tf_gemm_tc.cu", "tf_simt.cu"]
+LIB_SOURCES = ["tf_api.cu", "tf_gemm_tc.cu", "tf_gemm_2sm.cu", "tf_simt.cu"]
 
 
 def nvcc() -> str:
@@ -35,7 +35,7 @@ def nvcc() -> str:
 
 def _flags() -> list[str]:
     return ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
-                   "-I", str(ROOT / "include"), "--expt-relaxed-constexpr"]
+                   "-I", str(ROOT / "include")]
 
 
 def _newer(target: pathlib.Path, deps: list[pathlib.Path]) -> bool:

@@ -34,7 +34,7 @@
 #include <string>
 #include <vector>
 
-#include "../../../include/tforge.h"
+#include "tforge.h"
 
 namespace {
 

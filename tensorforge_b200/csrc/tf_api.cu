@@ -14,7 +14,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/tforge.h"
+#include "tforge.h"
 #include "tf_internal.h"
 
 using namespace tf;
@@ -151,32 +151,43 @@ struct Choice {
   TcConfig tc;
 };
 
-// Number of CTAs of an M x N problem for a BN-wide tile (BM = 128).
-int64_t ctas(int64_t M, int64_t N, int bn) { return ((M + 127) / 128) * ((N + bn - 1) / bn); }
+// Stages per instantiated configuration: [prec][bn index] for one CTA; pair kernel.
+constexpr int kStages1[3][3] = {{4, 6, 8}, {2, 3, 4}, {4, 6, 8}};  // bn = 256, 128, 64
+constexpr int kStagesPair[3] = {6, 4, 6};                          // TF32, X3, BF16
+
+// Relative throughput per busy SM of each kernel shape (pair, bn 256, 128, 64): wider
+// tiles read fewer operand bytes per FLOP, and the pair halves B per SM.
+constexpr double kKernelEff[4] = {1.0, 0.6, 0.5, 0.4};
+
+// Estimated time units of a configuration: waves of CTAs (148 SMs, one CTA each) over
+// the useful fraction of the tile area, divided by the per-SM throughput factor.
+double est_cost(int64_t M, int64_t N, int tile_m, int tile_n, int ctas_per_tile, double eff) {
+  const int64_t tiles = ((M + tile_m - 1) / tile_m) * ((N + tile_n - 1) / tile_n);
+  const int64_t ctas = tiles * ctas_per_tile;
+  const double waves = (double)((ctas + 147) / 148);
+  const double area = (double)tiles * tile_m * tile_n;  // MMA work incl. padding
+  const double per_wave_area = 148.0 / ctas_per_tile * tile_m * tile_n;
+  return (waves * per_wave_area > area ? waves * per_wave_area : area) / eff;
+}
 
 TcConfig table_tc(int prec, int64_t M, int64_t N, int64_t K) {
   (void)K;
-  // Prefer the widest tile (least operand traffic per FLOP) unless a narrower one fills
-  // the 148 SMs noticeably better: compare the fraction of the last wave that is busy.
+  TcConfig best{prec, 256, kStagesPair[prec], 1};
+  double best_cost = est_cost(M, N, 256, 256, 2, kKernelEff[0]);
   const int bns[3] = {256, 128, 64};
-  const int st[3][3] = {{4, 6, 8}, {2, 3, 4}, {4, 6, 8}};  // [prec][bn index]
-  int best = 0;
-  double best_score = -1;
   for (int i = 0; i < 3; ++i) {
-    const int64_t c = ctas(M, N, bns[i]);
-    const double waves = (double)c / 148.0;
-    const double eff = waves / (double)((c + 147) / 148);  // SM-slot utilisation
-    // Columns of the last N tile that hold no output are wasted MMA work.
-    const double n_eff = (double)N / (double)(((N + bns[i] - 1) / bns[i]) * bns[i]);
-    // Narrower tiles cost operand bandwidth: weight by a per-width efficiency guess.
-    const double width_eff = bns[i] == 256 ? 1.0 : (bns[i] == 128 ? 0.9 : 0.75);
-    const double score = eff * n_eff * width_eff;
-    if (score > best_score + 1e-9) {
-      best_score = score;
-      best = i;
+    const double c = est_cost(M, N, 128, bns[i], 1, kKernelEff[i + 1]);
+    if (c < best_cost * (1 - 1e-9)) {
+      best_cost = c;
+      best = TcConfig{prec, bns[i], kStages1[prec][i], 0};
     }
   }
-  return TcConfig{prec, bns[best], st[prec][best]};
+  return best;
+}
+
+bool config_supported(const TcConfig &c) {
+  if (c.pair) return c.bn == 256 && pair_smem_bytes(c.prec, c.stages) > 0;
+  return tc_config_supported(c);
 }
 
 Choice choose(int mode, int64_t M, int64_t N, int64_t K, bool tma_ok) {
@@ -191,9 +202,12 @@ Choice choose(int mode, int64_t M, int64_t N, int64_t K, bool tma_ok) {
   std::lock_guard<std::mutex> lk(g_cfg_mu);
   if (g_cfg.kernel == 2) {
     c.kind = K_SIMT;
-  } else if (g_cfg.kernel == 1) {
-    TcConfig f{prec, g_cfg.bn ? g_cfg.bn : c.tc.bn, g_cfg.stages ? g_cfg.stages : c.tc.stages};
-    if (tc_config_supported(f)) c.tc = f;
+  } else if (g_cfg.kernel == 1 || g_cfg.kernel == 3) {
+    const int pair = g_cfg.kernel == 3;
+    TcConfig f{prec, pair ? 256 : (g_cfg.bn ? g_cfg.bn : (c.tc.pair ? 256 : c.tc.bn)), 0, pair};
+    f.stages = g_cfg.stages ? g_cfg.stages
+                            : (pair ? kStagesPair[prec] : kStages1[prec][f.bn == 256 ? 0 : (f.bn == 128 ? 1 : 2)]);
+    if (config_supported(f)) c.tc = f;
     else c.kind = -1;
   }
   return c;
@@ -266,7 +280,8 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   p.limit_ns = g_wait_limit_ns.load();
   p.debug_skip = g_debug_skip.load();
   const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
-  cudaError_t e = launch_gemm_tc(cfg, epi, tmA, tmB, p, st);
+  cudaError_t e = cfg.pair ? launch_gemm_pair(cfg.prec, cfg.stages, epi, tmA, tmB, p, st)
+                           : launch_gemm_tc(cfg, epi, tmA, tmB, p, st);
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
   return TFORGE_OK;
 }
@@ -452,22 +467,25 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
     return TFORGE_OK;
   }
   static const char *names[3] = {"tf_gemm_tcgen05_tf32", "tf_gemm_tcgen05_3xtf32", "tf_gemm_tcgen05_bf16"};
-  std::snprintf(out->kernel, sizeof(out->kernel), "%s", names[c.tc.prec]);
-  out->grid[0] = (int)((N + c.tc.bn - 1) / c.tc.bn);
-  out->grid[1] = (int)((M + 127) / 128);
+  std::snprintf(out->kernel, sizeof(out->kernel), "%s%s", names[c.tc.prec], c.tc.pair ? "_pair" : "");
+  const int tm = c.tc.pair ? 256 : 128;
+  out->grid[0] = (int)((N + c.tc.bn - 1) / c.tc.bn) * (c.tc.pair ? 2 : 1);
+  out->grid[1] = (int)((M + tm - 1) / tm);
   out->grid[2] = 1;
   out->block[0] = 256;
   out->block[1] = out->block[2] = 1;
-  out->smem_bytes = tc_smem_bytes(c.tc);
-  out->tile[0] = 128;
+  out->cluster[0] = c.tc.pair ? 2 : 1;
+  out->smem_bytes = c.tc.pair ? pair_smem_bytes(c.tc.prec, c.tc.stages) : tc_smem_bytes(c.tc);
+  out->tile[0] = tm;
   out->tile[1] = c.tc.bn;
   out->tile[2] = c.tc.prec == PREC_BF16 ? 64 : 32;
   out->stages = c.tc.stages;
-  out->tmem_cols = c.tc.bn;
+  out->tmem_cols = c.tc.pair ? pair_tmem_cols(c.tc.prec) : c.tc.bn;
   if (have_dev) {
     cudaFuncAttributes fa{};
     int blocks = 0;
-    cudaError_t e = tc_func_attributes(c.tc, epi, &fa, &blocks);
+    cudaError_t e = c.tc.pair ? pair_func_attributes(c.tc.prec, c.tc.stages, epi, &fa, &blocks)
+                              : tc_func_attributes(c.tc, epi, &fa, &blocks);
     fill_attrs(e, fa, blocks);
   }
   return TFORGE_OK;
@@ -479,7 +497,7 @@ int tforge_set_config(const tforge_config *cfg) {
     g_cfg = tforge_config{};
     return TFORGE_OK;
   }
-  if (cfg->kernel < 0 || cfg->kernel > 2) return TFORGE_ERR_MODE;
+  if (cfg->kernel < 0 || cfg->kernel > 3) return TFORGE_ERR_MODE;
   g_cfg = *cfg;
   return TFORGE_OK;
 }

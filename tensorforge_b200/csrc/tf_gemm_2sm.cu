@@ -1,0 +1,421 @@
+// tf_gemm_2sm.cu -- fused GEMM on a CTA pair (tcgen05 cta_group::2), 256 x 256 output tiles.
+//
+// Same operator and epilogue as tf_gemm_tc.cu (matmul, mbr = relu(A @ B + bias),
+// matmul_add), for large problems.  Two CTAs on two SMs form a cluster; CTA r of the pair
+// loads A rows [m0 + 128 r, +128) and B columns [n0 + 128 r, +128) into its own shared
+// memory (plain TMA tile loads, no multicast), and one pair MMA (M = 256, N = 256) reads
+// A from both CTAs and B from both halves, so each SM reads only half of B per FLOP.
+//
+// fp32-accurate mode (3xTF32): per K step the MMA issues lo*hi, hi*lo and hi*hi.  The
+// split of A goes to tensor memory (tcgen05.st), so A crosses shared memory once and the
+// MMAs read only B from shared memory.  384 threads per CTA:
+//
+//   warp 0       TMA producer (each CTA): A tile and B half of each stage -> full[s].
+//   warps 2..11  converters (each CTA): the B half is split into hi (in place) and lo (a
+//                second buffer); warps 4..11 also split A: warp w takes rows
+//                32 (w % 4) .. +31 (its TMEM lane quadrant) and K half (w - 4) / 4, into
+//                TMEM columns [256 + 64 s, +32) (hi) and [+32, +32) (lo).  Then each warp
+//                arrives on this CTA's conv[s].
+//   warp 1       leader CTA: issues the pair MMAs into TMEM columns [0, 256) of both CTAs
+//                once its conv[s] and ready[s] (the peer's) completed; a multicast
+//                tcgen05.commit frees stage s in both CTAs (empty[s]), a last one signals
+//                accf in both.  Peer CTA: relays its conv[s] to the leader's ready[s] with
+//                one remote arrive per stage.
+//   warps 4..11  epilogue (each CTA): its 128 rows x 256 columns from its own TMEM.
+//
+// The split (kPairSplit): the tensor core reads an f32 operand as TF32 by dropping its low
+// 13 mantissa bits, so the truncation split keeps hi = x (no store) and computes only
+// lo = x - trunc(x), exact in f32.  The round split (cvt.rna) is kept as an alternative.
+//
+// TF32 / BF16 modes have no converters: each CTA's TMA (.cta_group::2 form) completes on
+// the LEADER's full[s], which expects both CTAs' bytes, and the MMA reads A and B from
+// shared memory.
+//
+// Every wait is bounded (tf_ptx.cuh); both CTAs meet at a cluster barrier before TMEM is
+// freed, so no CTA exits while the pair MMA may still read its shared or tensor memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "tf_internal.h"
+#include "tf_ptx.cuh"
+
+namespace tf {
+
+#ifndef TF_PAIR_SPLIT
+#define TF_PAIR_SPLIT 1
+#endif
+// 3xTF32 operand split of the pair kernel: 1 = truncation split, 0 = round split.
+constexpr int kPairSplit = TF_PAIR_SPLIT;
+
+namespace {
+
+template <int PREC, int STAGES>
+struct PairLayout {
+  static constexpr int kThreads = PREC == PREC_X3 ? 384 : 256;
+  static constexpr int kElem = PREC == PREC_BF16 ? 2 : 4;
+  static constexpr int kBK = 128 / kElem;              // K elements per stage (one 128-B row)
+  static constexpr int kUmmaK = 32 / kElem;            // K per MMA instruction
+  static constexpr int kKSteps = kBK / kUmmaK;         // 4
+  static constexpr int kNBlk = 128 / kElem;            // N elements per 128-B MN block
+  static constexpr int kBNHalf = 128;                  // B columns loaded by each CTA
+  static constexpr int kBBlocks = kBNHalf / kNBlk;     // TMA boxes per B half
+  static constexpr uint32_t kBSwz = kElem == 4 ? 1u : 2u;
+  static constexpr uint32_t kBSbo = kElem == 4 ? 512u : 1024u;
+  static constexpr int kABytes = 128 * 128;            // this CTA's 128 A rows
+  static constexpr int kBBytes = kBNHalf * kBK * kElem;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kLoBytes = PREC == PREC_X3 ? kBBytes : 0;  // B lo (A lo lives in TMEM)
+  static constexpr int kRingBytes = STAGES * (kStageBytes + kLoBytes);
+  static constexpr int kNumBars = 4 * STAGES + 1;      // full, conv, ready, empty, accf
+  static constexpr int kBarBytes = 8 * kNumBars + 16;
+  static constexpr int kSmemBytes = 1024 + kRingBytes + kBarBytes;
+  static constexpr uint32_t kAccCols = 256;
+  static constexpr uint32_t kTmemCols = PREC == PREC_X3 ? 512u : 256u;
+  static constexpr int kConvWarps = 10;                // warps 2..11 (3xTF32)
+  __host__ __device__ static constexpr int a_off(int s) { return s * kStageBytes; }
+  __host__ __device__ static constexpr int b_off(int s) { return s * kStageBytes + kABytes; }
+  __host__ __device__ static constexpr int lo_off(int s) { return STAGES * kStageBytes + s * kLoBytes; }
+  __host__ __device__ static constexpr int bar_off() { return kRingBytes; }
+  __host__ __device__ static constexpr uint32_t a_tmem_col(int s) { return kAccCols + 64u * s; }
+  static_assert(PREC != PREC_X3 || kAccCols + 64u * STAGES <= 512u, "TMEM budget");
+};
+
+// Bounded pause (abort drains of loads this CTA cannot observe).
+__device__ __forceinline__ void pause_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer();
+  while (globaltimer() - t0 < ns) __nanosleep(1000);
+}
+
+template <int PREC, int STAGES, int EPI, int SPLIT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STAGES>::kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const TcParams p) {
+  using L = PairLayout<PREC, STAGES>;
+  constexpr bool kX3 = PREC == PREC_X3;
+  constexpr bool kTF32 = PREC != PREC_BF16;
+  constexpr uint32_t kIdesc = instr_desc(kTF32 ? 2u : 1u, 256, 256);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off());
+  // full[s]: TMA bytes landed (3xTF32: this CTA's; otherwise the leader's barrier counts
+  // both CTAs' bytes); conv[s]: this CTA's converters done; ready[s] (leader): the peer's
+  // converters done; empty[s]: the pair MMAs reading stage s done; accf: accumulator done.
+  const uint32_t full0 = smem_u32(bars), conv0 = full0 + 8 * STAGES, ready0 = conv0 + 8 * STAGES,
+                 empty0 = ready0 + 8 * STAGES, accf = empty0 + 8 * STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int n0 = (blockIdx.x >> 1) * 256, m0 = blockIdx.y * 256 + (int)rank * 128;
+  const int nkb = (p.K + L::kBK - 1) / L::kBK;
+  const WaitCtl wc{abort_flag, p.status, p.limit_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(conv0 + 8 * s, L::kConvWarps);
+      mbar_init(ready0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(accf, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any remote arrive or TMA
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    // 3xTF32: loads complete on this CTA's full[s] (its converters consume them).
+    // TF32/BF16: loads complete on the LEADER's full[s], which expects both CTAs' bytes.
+    const uint32_t lead_full0 = map_to_cta(full0, 0);
+    int kb = 0;
+    for (; kb < nkb; ++kb) {
+      const int s = kb % STAGES, round = kb / STAGES;
+      if (round > 0 && !mbar_wait_cluster(empty0 + 8 * s, (round - 1) & 1, wc)) break;
+      if (p.debug_skip && kb == 0) continue;  // test hook: this stage never fills
+      const int kc = kb * L::kBK;
+      const int nb = n0 + (int)rank * L::kBNHalf;
+      if constexpr (kX3) {
+        mbar_arrive_expect_tx(full0 + 8 * s, L::kStageBytes);
+        tma_load_2d(sbase + L::a_off(s), &tmA, kc, m0, full0 + 8 * s);
+#pragma unroll
+        for (int j = 0; j < L::kBBlocks; ++j)
+          tma_load_2d(sbase + L::b_off(s) + j * (L::kBK * 128), &tmB, nb + j * L::kNBlk, kc, full0 + 8 * s);
+      } else {
+        if (rank == 0) mbar_arrive_expect_tx(full0 + 8 * s, 2 * L::kStageBytes);
+        tma_load_2d_pair(sbase + L::a_off(s), &tmA, kc, m0, lead_full0 + 8 * s);
+#pragma unroll
+        for (int j = 0; j < L::kBBlocks; ++j)
+          tma_load_2d_pair(sbase + L::b_off(s) + j * (L::kBK * 128), &tmB, nb + j * L::kNBlk, kc,
+                           lead_full0 + 8 * s);
+      }
+    }
+    if (*abort_flag) {
+      if (kX3 || rank == 0) {
+#pragma unroll 1
+        for (int s = 0; s < STAGES; ++s) {
+          if (kb - 1 < s) continue;
+          const int last = kb - 1 - ((kb - 1 - s) % STAGES);
+          if (p.debug_skip && last == 0) continue;
+          mbar_wait_drain_cluster(full0 + 8 * s, (last / STAGES) & 1, p.limit_ns);
+        }
+      } else {
+        pause_ns(200000);  // the peer's loads complete on the leader's barrier
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    if (rank == 0) {
+      // ---------------- pair MMA issuer (leader CTA) ----------------
+      uint32_t accum = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES, round = kb / STAGES;
+        if constexpr (kX3) {
+          if (!mbar_wait(conv0 + 8 * s, round & 1, wc)) break;
+          if (!mbar_wait_cluster(ready0 + 8 * s, round & 1, wc)) break;
+        } else {
+          if (!mbar_wait_cluster(full0 + 8 * s, round & 1, wc)) break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < L::kKSteps; ++ks) {
+          const uint64_t bd = smem_desc(sbase + L::b_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
+                                        L::kBSbo, L::kBSwz);
+          if constexpr (kX3) {
+            const uint32_t a_hi = tmem + L::a_tmem_col(s) + 8 * ks, a_lo = a_hi + 32;
+            const uint64_t bl = smem_desc(sbase + L::lo_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
+                                          L::kBSbo, L::kBSwz);
+            mma_ts_pair_tf32(tmem, a_lo, bd, kIdesc, accum);
+            mma_ts_pair_tf32(tmem, a_hi, bl, kIdesc, 1u);
+            mma_ts_pair_tf32(tmem, a_hi, bd, kIdesc, 1u);
+          } else {
+            const uint64_t ad = smem_desc(sbase + L::a_off(s) + ks * 32, 16, 1024, 2);
+            mma_ss_pair<kTF32>(tmem, ad, bd, kIdesc, accum);
+          }
+          accum = 1u;
+        }
+        mma_commit_pair(empty0 + 8 * s, 0x3);
+      }
+      mma_commit_pair(accf, 0x3);
+      if (*abort_flag) mbar_wait_drain_cluster(accf, 0, p.limit_ns);
+    } else if constexpr (kX3) {
+      // ---------------- relay (peer CTA): conv[s] -> leader's ready[s] ----------------
+      const uint32_t lead_ready0 = map_to_cta(ready0, 0);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES, round = kb / STAGES;
+        if (!mbar_wait(conv0 + 8 * s, round & 1, wc)) break;
+        mbar_arrive_cluster(lead_ready0 + 8 * s);
+      }
+    }
+  } else if (kX3 && warp >= 2) {
+    // ---------------- 3xTF32 converters (both CTAs, warps 2..11) ----------------
+    const int t = threadIdx.x - 64;
+    constexpr int kChunks = L::kBBytes / 16;
+    const int q = warp & 3, h = (warp - 4) >> 2, r = q * 32 + lane;  // A: row r, K half h
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % STAGES, round = kb / STAGES;
+      if (!mbar_wait(full0 + 8 * s, round & 1, wc)) break;
+      float4 *braw = reinterpret_cast<float4 *>(smem + L::b_off(s));
+      float4 *blo = reinterpret_cast<float4 *>(smem + L::lo_off(s));
+#pragma unroll 2
+      for (int c = t; c < kChunks; c += 320) {
+        const float4 x = braw[c];
+        float4 l;
+        if constexpr (SPLIT == 1) {
+          l.x = split_lo_trunc(x.x); l.y = split_lo_trunc(x.y);
+          l.z = split_lo_trunc(x.z); l.w = split_lo_trunc(x.w);
+          const uint4 u = make_uint4(__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z),
+                                     __float_as_uint(x.w));
+          const uint4 hu = make_uint4(split_hi_trunc_bits(u.x), split_hi_trunc_bits(u.y),
+                                      split_hi_trunc_bits(u.z), split_hi_trunc_bits(u.w));
+          if ((hu.x ^ u.x) | (hu.y ^ u.y) | (hu.z ^ u.z) | (hu.w ^ u.w))  // a NaN to quiet (rare)
+            braw[c] = make_float4(__uint_as_float(hu.x), __uint_as_float(hu.y), __uint_as_float(hu.z),
+                                  __uint_as_float(hu.w));
+        } else {
+          float4 hh;
+          hh.x = to_tf32(x.x); hh.y = to_tf32(x.y); hh.z = to_tf32(x.z); hh.w = to_tf32(x.w);
+          l.x = isfinite(hh.x) ? to_tf32(x.x - hh.x) : 0.f;
+          l.y = isfinite(hh.y) ? to_tf32(x.y - hh.y) : 0.f;
+          l.z = isfinite(hh.z) ? to_tf32(x.z - hh.z) : 0.f;
+          l.w = isfinite(hh.w) ? to_tf32(x.w - hh.w) : 0.f;
+          braw[c] = hh;
+        }
+        blo[c] = l;
+      }
+      fence_proxy_async_smem();
+      if (warp >= 4) {
+        // Row r of the A tile (128 B at r * 128, 16-B chunk j stored at j ^ (r % 8)); this
+        // warp splits K elements [16 h, 16 h + 16) into TMEM columns of stage s.
+        const uint8_t *arow = smem + L::a_off(s) + r * 128;
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = 4 * h + jj;
+          const float4 v = *reinterpret_cast<const float4 *>(arow + ((j ^ (r & 7)) << 4));
+          const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if constexpr (SPLIT == 1) {
+              hi[4 * jj + i] = split_hi_trunc_bits(__float_as_uint(xs[i]));
+              lo[4 * jj + i] = __float_as_uint(split_lo_trunc(xs[i]));
+            } else {
+              const float hv = to_tf32(xs[i]);
+              hi[4 * jj + i] = __float_as_uint(hv);
+              lo[4 * jj + i] = __float_as_uint(isfinite(hv) ? to_tf32(xs[i] - hv) : 0.f);
+            }
+          }
+        }
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + L::a_tmem_col(s) + 16 * h;
+        tmem_st_32x32b_x16(ta, hi);
+        tmem_st_32x32b_x16(ta + 32, lo);
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(conv0 + 8 * s);
+    }
+  }
+
+  // ---------------- epilogue: TMEM -> registers -> global (both CTAs) ----------------
+  if (warp >= 4) {
+    if (mbar_wait_cluster(accf, 0, wc, 128)) {
+      tc_fence_after();
+      const int q = warp & 3;
+      constexpr int kEpiWarps = L::kThreads / 32 - 4;     // 4 or 8
+      constexpr int kChunksPerWarp = 8 / (kEpiWarps / 4);  // column chunks of 32 per warp
+      const int c0 = ((warp - 4) >> 2) * kChunksPerWarp;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      float *orow = p.out + (int64_t)row * p.ldc;
+#pragma unroll 1
+      for (int c = c0; c < c0 + kChunksPerWarp; ++c) {
+        uint32_t rr[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, rr);
+        tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const int col = col0 + j;
+            if (col < p.N) {
+              float4 v = make_float4(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]),
+                                     __uint_as_float(rr[j + 2]), __uint_as_float(rr[j + 3]));
+              if constexpr (EPI == EPI_MBR) {
+                const float4 b = __ldg(reinterpret_cast<const float4 *>(p.bias + col));
+                v.x = relu_ieee(__fadd_rn(v.x, b.x));
+                v.y = relu_ieee(__fadd_rn(v.y, b.y));
+                v.z = relu_ieee(__fadd_rn(v.z, b.z));
+                v.w = relu_ieee(__fadd_rn(v.w, b.w));
+              } else if constexpr (EPI == EPI_ADD) {
+                const float4 cr = __ldg(reinterpret_cast<const float4 *>(p.cres + (int64_t)row * p.ldc + col));
+                v.x = __fadd_rn(v.x, cr.x);
+                v.y = __fadd_rn(v.y, cr.y);
+                v.z = __fadd_rn(v.z, cr.z);
+                v.w = __fadd_rn(v.w, cr.w);
+              }
+              *reinterpret_cast<float4 *>(orow + col) = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while the pair MMA may still read its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, L::kTmemCols);
+  }
+}
+
+template <int PREC, int STAGES, int EPI>
+cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
+                            cudaStream_t stream) {
+  using L = PairLayout<PREC, STAGES>;
+  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit>;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
+  }
+  dim3 grid(2 * ((p.N + 255) / 256), (p.M + 255) / 256, 1);
+  kern<<<grid, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, p);
+  return cudaGetLastError();
+}
+
+template <int PREC, int STAGES>
+cudaError_t launch_pair_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
+                            cudaStream_t stream) {
+  switch (epi) {
+    case EPI_MATMUL: return launch_pair_one<PREC, STAGES, EPI_MATMUL>(tmA, tmB, p, stream);
+    case EPI_MBR: return launch_pair_one<PREC, STAGES, EPI_MBR>(tmA, tmB, p, stream);
+    case EPI_ADD: return launch_pair_one<PREC, STAGES, EPI_ADD>(tmA, tmB, p, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int PREC, int STAGES>
+cudaError_t pair_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
+  using L = PairLayout<PREC, STAGES>;
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit>)
+                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit>);
+  cudaError_t e = cudaFuncGetAttributes(a, f);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, f, L::kThreads, L::kSmemBytes);
+}
+
+}  // namespace
+
+// Instantiated pair configurations: (precision, stages).
+#define TF_PAIR_CONFIGS(X) X(PREC_X3, 4) X(PREC_TF32, 6) X(PREC_BF16, 6)
+
+int pair_smem_bytes(int prec, int stages) {
+#define TF_PSMEM(P, S) \
+  if (prec == P && stages == S) return PairLayout<P, S>::kSmemBytes;
+  TF_PAIR_CONFIGS(TF_PSMEM)
+#undef TF_PSMEM
+  return -1;
+}
+
+int pair_tmem_cols(int prec) { return prec == PREC_X3 ? 512 : 256; }
+
+cudaError_t launch_gemm_pair(int prec, int stages, int epi, const CUtensorMap &tmA,
+                             const CUtensorMap &tmB, const TcParams &p, cudaStream_t stream) {
+#define TF_PLAUNCH(P, S) \
+  if (prec == P && stages == S) return launch_pair_epi<P, S>(epi, tmA, tmB, p, stream);
+  TF_PAIR_CONFIGS(TF_PLAUNCH)
+#undef TF_PLAUNCH
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t pair_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *a, int *blocks) {
+#define TF_PATTR(P, S) \
+  if (prec == P && stages == S) return pair_attrs<P, S>(epi, a, blocks);
+  TF_PAIR_CONFIGS(TF_PATTR)
+#undef TF_PATTR
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace tf

@@ -52,10 +52,10 @@ struct TcLayout {
   static constexpr int kBarBytes = 8 * (3 * STAGES + 1) + 16;
   static constexpr int kSmemBytes = 1024 + kRingBytes + kBarBytes;
   // Shared-memory offsets (relative to the 1024-aligned base).
-  static constexpr int a_off(int s) { return s * kStageBytes; }
-  static constexpr int b_off(int s) { return s * kStageBytes + kABytes; }
-  static constexpr int lo_off(int s) { return STAGES * kStageBytes + s * kLoBytes; }
-  static constexpr int bar_off() { return kRingBytes; }
+  __host__ __device__ static constexpr int a_off(int s) { return s * kStageBytes; }
+  __host__ __device__ static constexpr int b_off(int s) { return s * kStageBytes + kABytes; }
+  __host__ __device__ static constexpr int lo_off(int s) { return STAGES * kStageBytes + s * kLoBytes; }
+  __host__ __device__ static constexpr int bar_off() { return kRingBytes; }
 };
 
 template <int PREC, int BN, int STAGES, int EPI>

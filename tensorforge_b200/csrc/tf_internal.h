@@ -25,8 +25,9 @@ struct TcParams {
 
 struct TcConfig {
   int prec;    // Prec
-  int bn;      // 64, 128, 256
+  int bn;      // 64, 128, 256 (output tile width; 256 for the CTA-pair kernel)
   int stages;
+  int pair;    // 1: CTA-pair kernel (cta_group::2, 256 x 256 tiles), 0: one CTA per 128 x bn tile
 };
 
 // Dynamic shared memory the tcgen05 kernel needs for a configuration.
@@ -42,6 +43,14 @@ cudaError_t launch_gemm_tc(const TcConfig &cfg, int epi, const CUtensorMap &tmA,
 cudaError_t tc_func_attributes(const TcConfig &cfg, int epi, cudaFuncAttributes *attr,
                                int *blocks_per_sm);
 cudaError_t simt_func_attributes(int epi, cudaFuncAttributes *attr, int *blocks_per_sm);
+
+// CTA-pair (cta_group::2) kernel: 256 x 256 output tiles, clusters of two CTAs.
+int pair_smem_bytes(int prec, int stages);
+int pair_tmem_cols(int prec);
+cudaError_t launch_gemm_pair(int prec, int stages, int epi, const CUtensorMap &tmA,
+                             const CUtensorMap &tmB, const TcParams &p, cudaStream_t stream);
+cudaError_t pair_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *attr,
+                                 int *blocks_per_sm);
 
 // SIMT sequential-k FFMA GEMM (bitwise equal to the reference's generated kernels).
 cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const float *aux, float *C,

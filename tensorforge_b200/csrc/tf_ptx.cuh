@@ -55,7 +55,7 @@ struct WaitCtl {
   uint64_t limit_ns;
 };
 
-__device__ __noinline__ void raise_timeout(const WaitCtl &c) {
+static __device__ __noinline__ void raise_timeout(const WaitCtl &c) {
   *c.abort = 1u;
   atomicCAS(c.status, 0u, kStatusTimeout);
 }
@@ -96,6 +96,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int3
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+// CTA-pair form: the tile lands in this CTA's shared memory at `dst`; completion is
+// counted on the mbarrier at cluster address `bar_cluster`, which may be in the peer CTA
+// of the pair (the leader's barrier collects both CTAs' bytes).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *tmap, int32_t c0, int32_t c1,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar_cluster)
       : "memory");
 }
 
@@ -167,6 +179,140 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---- clusters and CTA pairs -----------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// Arrive (release, cluster scope) on an mbarrier of any CTA in the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// try_wait with acquire at cluster scope (barriers that peers or pair commits arrive on).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded cluster-scope wait; `sleep_ns` > 0 backs off between polls (long waits).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const WaitCtl &c,
+                                                  uint32_t sleep_ns = 0) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i) {
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+      if (sleep_ns) __nanosleep(sleep_ns);
+    }
+    if (*c.abort) return false;
+    if (globaltimer() - t0 > c.limit_ns) {
+      raise_timeout(c);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait_drain_cluster(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+}
+
+// ---- tcgen05, CTA pair (cta_group::2) ------------------------------------------------
+// Both CTAs of the pair execute alloc / relinquish / dealloc from the same warp.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// Pair MMA, A and B from shared memory (each CTA supplies its A rows and its half of B).
+template <bool kTF32>
+__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  if constexpr (kTF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+// Pair MMA, A from tensor memory (each CTA's own TMEM, same address), B from shared memory.
+__device__ __forceinline__ void mma_ts_pair_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier at `bar` in every CTA of `cta_mask` when all pair MMAs
+// issued so far by this thread have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive columns from registers: thread t writes lane (base lane + t).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+      "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
+      "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// 32 lanes x 16 consecutive columns.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // ---- descriptors --------------------------------------------------------------------
 // Shared-memory matrix descriptor (sm_100): start >> 4 in [0,14), leading byte offset
 // >> 4 in [16,30), stride byte offset >> 4 in [32,46), version 1 at bit 46, swizzle
@@ -187,8 +333,28 @@ __host__ __device__ constexpr uint32_t instr_desc(uint32_t fmt, uint32_t m, uint
 
 // IEEE-2019 maximum(x, +0.0): a NaN input is returned unchanged (payload kept, as the
 // reference's fold keeps 0x7FC00000, test/Transforms/canonicalize.mlir:90-100), -0.0 and
-// negatives give +0.0.
-__device__ __forceinline__ float relu_ieee(float x) { return (x > 0.0f || x != x) ? x : 0.0f; }
+// negatives give +0.0.  Written on the bit pattern: a float compare-and-select may be
+// contracted into a max instruction that returns the canonical NaN instead.
+__device__ __forceinline__ float relu_ieee(float x) {
+  const uint32_t u = __float_as_uint(x);
+  const bool keep = static_cast<int32_t>(u) > 0 || (u & 0x7FFFFFFFu) > 0x7F800000u;  // > +0 or NaN
+  return __uint_as_float(keep ? u : 0u);
+}
+
+// ---- 3xTF32 operand split -----------------------------------------------------------
+// Round split: hi = tf32_rna(x), lo = tf32_rna(x - hi); the tensor core reads both exactly.
+// Truncation split, for tensor cores that read an f32 operand as TF32 by discarding its
+// low 13 mantissa bits: hi is x itself (read as trunc(x)), lo = x - trunc(x), which is
+// exact in f32 and is read truncated to 11 significant bits.  Non-finite x: lo = 0, and a
+// NaN whose payload lies only in the low 13 bits gets its quiet bit set so it is not read
+// as an infinity.
+__device__ __forceinline__ float split_lo_trunc(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return ((u & 0x7F800000u) == 0x7F800000u) ? 0.0f : __fsub_rn(x, __uint_as_float(u & 0xFFFFE000u));
+}
+__device__ __forceinline__ uint32_t split_hi_trunc_bits(uint32_t u) {
+  return ((u & 0x7FFFFFFFu) > 0x7F800000u) ? (u | 0x00400000u) : u;
+}
 
 // Round-to-nearest (ties away) to tf32: the result is an f32 with the low 13 bits zero.
 __device__ __forceinline__ float to_tf32(float x) {

@@ -22,8 +22,13 @@ namespace {
 
 constexpr int SBM = 128, SBN = 128, SBK = 8, STM = 8, STN = 8;
 
-// IEEE-2019 maximum(x, +0.0) with the NaN payload kept (see relu_ieee in tf_ptx.cuh).
-__device__ __forceinline__ float relu_max(float x) { return (x > 0.0f || x != x) ? x : 0.0f; }
+// IEEE-2019 maximum(x, +0.0) with the NaN payload kept, on the bit pattern (a float
+// compare-and-select may be contracted into a max that canonicalizes NaN).
+__device__ __forceinline__ float relu_max(float x) {
+  const uint32_t u = __float_as_uint(x);
+  const bool keep = static_cast<int32_t>(u) > 0 || (u & 0x7FFFFFFFu) > 0x7F800000u;  // > +0 or NaN
+  return __uint_as_float(keep ? u : 0u);
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const float *__restrict__ A,

@@ -74,9 +74,11 @@ def test_pitch_smaller_than_row_is_rejected():
 
 
 @pytest.mark.parametrize("shape,mode,kernel", [
-    ((2048, 2048, 2048), "fp32", "tf_gemm_tcgen05_3xtf32"),
-    ((2048, 2048, 2048), "tf32", "tf_gemm_tcgen05_tf32"),
-    ((2048, 2048, 2048), "bf16", "tf_gemm_tcgen05_bf16"),
+    ((2048, 2048, 2048), "fp32", "tf_gemm_tcgen05_3xtf32_pair"),
+    ((2048, 2048, 2048), "tf32", "tf_gemm_tcgen05_tf32_pair"),
+    ((2048, 2048, 2048), "bf16", "tf_gemm_tcgen05_bf16_pair"),
+    ((256, 256, 128), "fp32", "tf_gemm_tcgen05_3xtf32"),
+    ((300, 8, 64), "tf32", "tf_gemm_tcgen05_tf32"),
     ((2048, 2048, 2048), "fp32_exact", "tf_gemm_simt_ffma"),
     ((777, 1111, 333), "fp32", "tf_gemm_simt_ffma"),   # pitches not 16-byte multiples
     ((256, 256, 8), "fp32", "tf_gemm_simt_ffma"),      # K < 16: exact kernel keeps the fp32 bound
@@ -88,22 +90,29 @@ def test_dispatch_table(shape, mode, kernel):
     assert d["block"] == [256, 1, 1]
     if kernel.startswith("tf_gemm_tcgen05"):
         m, n, _ = shape
-        assert d["grid"] == [-(-n // d["tile"][1]), -(-m // 128), 1]
+        pair = kernel.endswith("_pair")
+        assert d["grid"] == [-(-n // d["tile"][1]) * (2 if pair else 1), -(-m // d["tile"][0]), 1]
+        assert d["cluster"] == [2 if pair else 1, 1, 1]
         assert d["smem_bytes"] <= 232448
-        assert d["tmem_cols"] == d["tile"][1]
+        assert d["tmem_cols"] <= 512
+        if not pair:
+            assert d["tmem_cols"] == d["tile"][1]
 
 
 def test_forced_config_and_reset():
     _lib.set_config(1, 128, 6)
     try:
         d = _lib.describe("mbr", 2048, 2048, 2048, "tf32")
-        assert d["tile"][1] == 128 and d["stages"] == 6
+        assert d["tile"] == [128, 128, 32] and d["stages"] == 6
+        _lib.set_config(3)  # CTA-pair kernel
+        d = _lib.describe("mbr", 256, 256, 128, "fp32")
+        assert d["kernel"] == "tf_gemm_tcgen05_3xtf32_pair" and d["tmem_cols"] == 512
         _lib.set_config(1, 96, 6)  # not instantiated
         with pytest.raises(_lib.TforgeError):
             _lib.describe("mbr", 2048, 2048, 2048, "tf32")
     finally:
         _lib.set_config()
-    assert _lib.describe("mbr", 2048, 2048, 2048, "tf32")["tile"][1] == 256
+    assert _lib.describe("mbr", 2048, 2048, 2048, "tf32")["kernel"] == "tf_gemm_tcgen05_tf32_pair"
 
 
 def test_compile_kernel_writes_launch_json(tmp_path, monkeypatch):

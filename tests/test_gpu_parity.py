@@ -199,3 +199,80 @@ def test_shim_check_matches_reference_api(gpu):
         assert res["pass"] and out.shape == (256, 256)
     res, out = tg.check("relu", 64, 48, 1)
     assert res["pass"]
+
+
+PAIR_SHAPES = [(256, 256, 32), (300, 520, 200), (1000, 1000, 1000), (512, 256, 2048), (257, 260, 36),
+               (2048, 2048, 2048)]
+
+
+@pytest.mark.parametrize("shape", PAIR_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
+@pytest.mark.parametrize("workload", ["mbr", "matmul_add"])
+def test_pair_kernel_within_bound(gpu, workload, mode, shape):
+    """The CTA-pair (cta_group::2) kernel, forced, on ragged and full tiles."""
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 77)
+    _lib.set_config(3)
+    try:
+        # bf16 rows must be 16-byte multiples for TMA (N, K multiples of 8); otherwise the
+        # table routes the call to the exact SIMT kernel.
+        tma_ok = mode != "bf16" or (n % 8 == 0 and k % 8 == 0)
+        assert _lib.describe(workload, m, n, k, mode)["kernel"].endswith("_pair") == tma_ok
+        out = tg.run_op(workload, ins, m, n, k, mode)
+    finally:
+        _lib.set_config()
+    res = tc.check_output(workload, ins, out, mode)
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+
+
+def test_pair_kernel_bounded_wait(gpu):
+    """Timeout path of the pair kernel: both CTAs drain, status is TIMEOUT, next call is right."""
+    L = _lib.lib()
+    m, n, k = 512, 512, 256
+    ins = tc.make_inputs("mbr", m, n, k, 4)
+    a, b, bias = (tg.DeviceBuffer.upload(ins[x]) for x in ("a", "b", "bias"))
+    out = tg.DeviceBuffer(m * n * 4)
+    _lib.set_config(3)
+    try:
+        for mode in ("fp32", "tf32"):
+            assert L.tforge_set_wait_limit_ns(50_000_000) == 0
+            assert L.tforge_debug_skip_load(1) == 0
+            try:
+                _lib.gemm("mbr", a.addr, b.addr, out.addr, m, n, k, mode, bias=bias.addr)
+                assert _lib.device_status(None) == _lib.ERR_TIMEOUT
+            finally:
+                L.tforge_debug_skip_load(0)
+                L.tforge_set_wait_limit_ns(0)
+            _lib.gemm("mbr", a.addr, b.addr, out.addr, m, n, k, mode, bias=bias.addr)
+            assert _lib.device_status(None) == 0
+            assert tc.check_output("mbr", ins, out.download((m, n)), mode)["pass"]
+    finally:
+        _lib.set_config()
+        for x in (a, b, bias, out):
+            x.free()
+
+
+def test_tf32_operands_are_read_truncated(gpu):
+    """The truncation split of the 3xTF32 pair kernel relies on the tensor core reading an
+    f32 operand as TF32 by discarding its low 13 mantissa bits (not rounding): pin it.
+
+    One nonzero product per output: A[m, 0] = 1 + (m + 1) 2^-16 (m < 63: only discarded
+    bits set), B[0, n] = 1, so a truncating read gives exactly 1.0 and a rounding read
+    gives 1 + 2^-10 for m >= 31.  Then the same with the roles of A and B swapped."""
+    m, n, k = 128, 64, 32
+    a = np.zeros((m, k), np.float32)
+    b = np.zeros((k, n), np.float32)
+    a[:63, 0] = 1 + (np.arange(63) + 1) * 2.0 ** -16
+    b[0, :] = 1
+    _lib.set_config(1, 64, 8)
+    try:
+        out = tg.run_op("matmul", {"a": a, "b": b}, m, n, k, "tf32")
+        assert (out[:63] == 1.0).all(), out[:63, 0]
+        a2 = np.zeros((m, k), np.float32)
+        b2 = np.zeros((k, n), np.float32)
+        a2[:, 0] = 1
+        b2[0, :63] = 1 + (np.arange(63) + 1) * 2.0 ** -16
+        out2 = tg.run_op("matmul", {"a": a2, "b": b2}, m, n, k, "tf32")
+        assert (out2[:, :63] == 1.0).all(), out2[0]
+    finally:
+        _lib.set_config()
