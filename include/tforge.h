@@ -108,6 +108,19 @@ int tforge_add(const float *X, const float *Y, float *Z, int64_t M, int64_t N, v
  * repeated TFORGE_MODE_BF16 calls with b_dtype = TFORGE_BF16. */
 int tforge_convert_bf16(const float *x, uint16_t *y, int64_t n, void *stream);
 
+/* relu(A @ B + bias) in TFORGE_MODE_BF16 without allocating anything.  No counterpart in
+ * the reference.  For callers that must not allocate device memory during a call (a
+ * serving loop that reserves all of its memory up front and cannot risk an out-of-memory
+ * error or an allocator synchronisation mid-request, or a host framework that owns every
+ * device byte).  The f32 -> bf16 operand copies go to a 16 MiB static device array that
+ * every GPU loading this library keeps until exit: bf16(A) (rounded up to 256 bytes) plus
+ * bf16(B) must fit in 16 MiB (e.g. M = N = K = 2048), else TFORGE_ERR_SHAPE.  Needs K and
+ * N multiples of 8 and 16-byte-aligned pointers (else TFORGE_ERR_UNSUPPORTED /
+ * TFORGE_ERR_ALIGN).  Calls share the array: calls that overlap on the GPU race.  The
+ * first call on a device resolves the array's address; make it before any stream capture. */
+int tforge_mbr_bf16_noalloc(const float *A, const float *B, const float *bias, float *out, int64_t M,
+                            int64_t N, int64_t K, void *stream);
+
 /* Launch description: replaces the `tforge.launch = {kernel, grid, block, args}`
  * module attribute (lib/Transforms/Gpu.cpp:449-457,572-577) that python/tforge_gpu.py
  * parses into launch.json (:42-51,88-90).  Filled for the kernel the dispatch table

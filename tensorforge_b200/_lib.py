@@ -60,6 +60,7 @@ SIGNATURES = {
     "tforge_relu": (_I, [_P, _P, _I64, _I64, _P]),
     "tforge_add": (_I, [_P, _P, _P, _I64, _I64, _P]),
     "tforge_convert_bf16": (_I, [_P, _P, _I64, _P]),
+    "tforge_mbr_bf16_noalloc": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "tforge_describe": (_I, [_I, _I64, _I64, _I64, _I, C.POINTER(Launch)]),
     "tforge_set_config": (_I, [C.POINTER(Config)]),
     "tforge_device_status": (_I, [_P]),

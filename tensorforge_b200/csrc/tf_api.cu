@@ -288,6 +288,26 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
 
 }  // namespace
 
+namespace tf {
+
+// The tensor-core configuration tforge_gemm picks for (mode, M, N, K) with TMA-compatible
+// operands, or false when it would not use a tensor-core kernel.
+bool select_tc_config(int mode, int64_t M, int64_t N, int64_t K, TcConfig *out) {
+  const Choice c = choose(mode, M, N, K, true);
+  if (c.kind != K_TC) return false;
+  *out = c.tc;
+  return true;
+}
+
+int encode_operand_map(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols,
+                       int64_t ld, uint32_t box_cols, uint32_t box_rows, bool atom32) {
+  return make_tmap(m, base, bf16, rows, cols, ld, box_cols, box_rows, atom32);
+}
+
+void set_last_error(const char *msg) { g_last_error = msg; }
+
+}  // namespace tf
+
 extern "C" {
 
 int tforge_gemm(const tforge_gemm_args *a, void *stream) {

@@ -52,6 +52,13 @@ cudaError_t launch_gemm_pair(int prec, int stages, int epi, const CUtensorMap &t
 cudaError_t pair_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *attr,
                                  int *blocks_per_sm);
 
+// The dispatch table's tensor-core choice (false when it would not use tcgen05), the
+// TMA operand map encoder, and the per-thread error text (all defined in tf_api.cu).
+bool select_tc_config(int mode, int64_t M, int64_t N, int64_t K, TcConfig *out);
+int encode_operand_map(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols,
+                       int64_t ld, uint32_t box_cols, uint32_t box_rows, bool atom32);
+void set_last_error(const char *msg);
+
 // SIMT sequential-k FFMA GEMM (bitwise equal to the reference's generated kernels).
 cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const float *aux, float *C,
                              int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
