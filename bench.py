@@ -55,13 +55,23 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--mode", default="fp32", choices=["fp32", "tf32", "bf16", "fp32_exact"])
-    ap.add_argument("--m", type=int, default=2048, help="rows per GPU")
+    ap.add_argument("--m", type=int, default=2048, help="rows per GPU (weak scaling)")
+    ap.add_argument("--m-total", type=int, default=0,
+                    help="total rows split over the GPUs (strong scaling, e.g. 131072 for config 4)")
+    ap.add_argument("--dist", default="uniform", choices=["uniform", "normal"],
+                    help="uniform: U[-1,1]; normal: A, B ~ N(0, std 1/sqrt(K)), bias ~ N(0, 0.1) (config 4)")
     ap.add_argument("--n", type=int, default=2048)
     ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--shape", default="",
+                    help="MxNxK, same as --m/--n/--k (use this form under torchrun, whose own flags "
+                         "make --m/--n ambiguous abbreviations)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.shape:
+        args.m, args.n, args.k = (int(x) for x in args.shape.lower().split("x"))
+    return args
 
 
 def host_threads() -> int:
@@ -72,10 +82,11 @@ def host_threads() -> int:
 
 
 # ---------------------------------------------------------------- CPU restatement timing
-def cpu_restatement_tflops(m, n, k, seconds=10.0, max_reps=50):
-    """Time the CPU restatement of the reference kernel (oracle/, pinned to the reference's
-    published numerics) on all host threads, one single-threaded call per row slice, the
-    way the single-threaded reference kernel would use every core."""
+def restatement_runner(m, n, k, seed=0):
+    """(run, rows, ins, out): one call of the CPU restatement of the reference kernel
+    (oracle/, pinned to the reference's published numerics) on all host threads, one
+    single-threaded call per row slice, the way the single-threaded reference kernel would
+    use every core."""
     import concurrent.futures as cf
 
     import numpy as np
@@ -83,29 +94,38 @@ def cpu_restatement_tflops(m, n, k, seconds=10.0, max_reps=50):
     from tests import oracle_lib
     from tensorforge_b200 import tforge_cpu as tc
 
+    subprocess_build_oracle()
     threads = host_threads()
-    ins = tc.make_inputs("mbr", m, n, k, 0)
+    ins = tc.make_inputs("mbr", m, n, k, seed)
     a, b, bias = ins["a"], ins["b"], ins["bias"]
     out = np.empty((m, n), dtype=np.float32)
-    lib = oracle_lib._lib
     rows = [(i * m // threads, (i + 1) * m // threads) for i in range(threads)]
     rows = [r for r in rows if r[1] > r[0]]
+    ex = cf.ThreadPoolExecutor(max_workers=len(rows))
 
     def part(r):
         r0, r1 = r
-        lib.oracle_gemm(1, a[r0:].ctypes.data, b.ctypes.data, bias.ctypes.data, out[r0:].ctypes.data,
-                        r1 - r0, n, k, 1)
+        oracle_lib._lib.oracle_gemm(1, a[r0:].ctypes.data, b.ctypes.data, bias.ctypes.data,
+                                    out[r0:].ctypes.data, r1 - r0, n, k, 1)
 
+    def run():
+        list(ex.map(part, rows))
+
+    return run, rows, ins, out
+
+
+def cpu_restatement_tflops(m, n, k, seconds=10.0, max_reps=50):
+    """Median TFLOP/s of the restatement over a bounded sample (about `seconds` of CPU time)."""
+    run, rows, _, _ = restatement_runner(m, n, k)
+    run()  # warm-up
     times = []
-    with cf.ThreadPoolExecutor(max_workers=len(rows)) as ex:
-        list(ex.map(part, rows))  # warm-up
-        t_end = time.perf_counter() + seconds / max(1, len(rows)) * 1.0
-        while len(times) < max_reps:
-            t0 = time.perf_counter()
-            list(ex.map(part, rows))
-            times.append(time.perf_counter() - t0)
-            if time.perf_counter() > t_end and len(times) >= 3:
-                break
+    t_end = time.perf_counter() + seconds / max(1, len(rows))
+    while len(times) < max_reps:
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and len(times) >= 3:
+            break
     med = statistics.median(times)
     return 2.0 * m * n * k / med / 1e12, len(rows), len(times), med
 
@@ -115,36 +135,20 @@ def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    subprocess_build_oracle()
-    import numpy as np  # noqa: F401
-
-    m, n, k = args.m, args.n, args.k
-    from tests import oracle_lib
-    from tensorforge_b200 import tforge_cpu as tc
-    import concurrent.futures as cf
-
-    threads = host_threads()
-    ins = tc.make_inputs("mbr", m, n, k, 0)
-    a, b, bias = ins["a"], ins["b"], ins["bias"]
     import numpy as np
 
-    out = np.empty((m, n), dtype=np.float32)
-    rows = [(i * m // threads, (i + 1) * m // threads) for i in range(threads)]
-    rows = [r for r in rows if r[1] > r[0]]
+    from tensorforge_b200 import tforge_cpu as tc
 
-    def part(r):
-        r0, r1 = r
-        oracle_lib._lib.oracle_gemm(1, a[r0:].ctypes.data, b.ctypes.data, bias.ctypes.data,
-                                    out[r0:].ctypes.data, r1 - r0, n, k, 1)
-
+    m = args.m_total if args.m_total else args.m
+    n, k = args.n, args.k
+    run, rows, ins, out = restatement_runner(m, n, k)
+    for _ in range(args.warmup):
+        run()
     step_t = []
-    with cf.ThreadPoolExecutor(max_workers=len(rows)) as ex:
-        for _ in range(args.warmup):
-            list(ex.map(part, rows))
-        for _ in range(args.steps):
-            t0 = time.perf_counter()
-            list(ex.map(part, rows))
-            step_t.append(time.perf_counter() - t0)
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        step_t.append(time.perf_counter() - t0)
     total = sum(step_t)
     value = 2.0 * m * n * k * args.steps / total / 1e12
     res = tc.check_output("mbr", ins, out, "fp32_exact", rows=np.arange(0, m, max(1, m // 64)))
@@ -268,25 +272,43 @@ def ours(args):
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
-    m, n, k, mode = args.m, args.n, args.k, args.mode
+    from tensorforge_b200.shard import broadcast_weights, row_partition
+
+    n, k, mode = args.n, args.k, args.mode
+    strong = args.m_total > 0
+    if strong:
+        r0, r1 = row_partition(args.m_total, world, rank)
+        m = r1 - r0
+        m_total = args.m_total
+    else:
+        m, m_total = args.m, args.m * world
     # Inputs: A rows are this rank's shard (seed offset by rank); B and bias from rank 0.
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
-    A = torch.empty((m, k), device=dev, dtype=torch.float32).uniform_(-1, 1, generator=g)
+    A = torch.empty((m, k), device=dev, dtype=torch.float32)
     B = torch.empty((k, n), device=dev, dtype=torch.float32)
     bias = torch.empty((n,), device=dev, dtype=torch.float32)
+    if args.dist == "normal":
+        A.normal_(0.0, 1.0 / k ** 0.5, generator=g)
+    else:
+        A.uniform_(-1, 1, generator=g)
     if rank == 0:
         g0 = torch.Generator(device=dev)
         g0.manual_seed(7)
-        B.uniform_(-1, 1, generator=g0)
-        bias.uniform_(-1, 1, generator=g0)
+        if args.dist == "normal":
+            B.normal_(0.0, 1.0 / k ** 0.5, generator=g0)
+            bias.normal_(0.0, 0.1, generator=g0)
+        else:
+            B.uniform_(-1, 1, generator=g0)
+            bias.uniform_(-1, 1, generator=g0)
     bcast_ms = None
     if world > 1:
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        dist.broadcast(B, src=0)
-        dist.broadcast(bias, src=0)
-        torch.cuda.synchronize()
+        dist.barrier()  # communicator set-up is not part of the broadcast time
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    broadcast_weights(B, bias, src=0)  # once per weight set, outside the timed region
+    torch.cuda.synchronize()
+    if world > 1:
         bcast_ms = 1e3 * (time.perf_counter() - t0)
     out = torch.empty((m, n), device=dev, dtype=torch.float32)
     flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
@@ -329,7 +351,7 @@ def ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
     flops_rank = 2.0 * m * n * k
-    value = world * flops_rank * args.steps / (total_ms * 1e-3) / 1e12
+    value = 2.0 * m_total * n * k * args.steps / (total_ms * 1e-3) / 1e12
 
     # Correctness of the timed output (seeded row subset vs FP64, the reference's bound).
     rows = np.arange(0, m, max(1, m // 64))
@@ -353,7 +375,6 @@ def ours(args):
         comparators = cublas_comparator(m, n, k, A, B, bias, flush, stream) if mode in ("fp32", "fp32_exact") else {}
         cpu = None
         if not args.no_cpu_baseline and world == 1:
-            subprocess_build_oracle()
             v, cores, reps, med = cpu_restatement_tflops(m, n, k)
             cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                    "sample": f"full {m}x{n}x{k} mbr, {reps} timed reps (median {med:.3f} s), {cores} row slices "
@@ -361,12 +382,15 @@ def ours(args):
         e2e = None if args.no_e2e else e2e_measure(L, _lib, m, n, k, mode, A, B, bias, world, dev)
         result = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
                   "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-                  "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                  "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32",
                   "data": "synthetic",
-                  "config": {"workload": f"mbr relu(A@B+bias) {m}x{n}x{k} per GPU, mode {mode}"
+                  "config": {"workload": (f"mbr relu(A@B+bias) {m_total}x{n}x{k} split over {world} GPU(s)" if strong
+                                          else f"mbr relu(A@B+bias) {m}x{n}x{k} per GPU") +
+                                         f", mode {mode}"
                                          f"{' (3xTF32 split products, f32 accumulate)' if mode == 'fp32' else ''}, "
-                                         "A/B/bias U[-1,1]",
-                             "M_total": m * world, "N": n, "K": k, "mode": mode,
+                                         + ("A,B ~ N(0,1/sqrt(K)), bias ~ N(0,0.1)" if args.dist == "normal"
+                                            else "A/B/bias U[-1,1]"),
+                             "M_total": m_total, "M_rank0": m, "N": n, "K": k, "mode": mode,
                              "l2": "flushed before every step (256 MiB write outside the step's events)",
                              "parallelism": f"M-sharded rows over {world} GPU(s); B and bias NCCL-broadcast once "
                                             "before timing; outputs stay sharded",

@@ -276,3 +276,42 @@ def test_tf32_operands_are_read_truncated(gpu):
         assert (out2[:, :63] == 1.0).all(), out2[0]
     finally:
         _lib.set_config()
+
+
+def test_row_sharded_calls_cover_the_full_problem(gpu):
+    """Rank-style row blocks (uneven split of M) through shard.mbr_rows equal the bound-checked
+    full problem; every row is written exactly once."""
+    import torch
+    from tensorforge_b200.shard import WeightSet, all_partitions, mbr_rows
+
+    m, n, k = 1000, 512, 384
+    ins = tc.make_inputs("mbr", m, n, k, 21)
+    dev = torch.device("cuda", 0)
+    A = torch.from_numpy(ins["a"]).to(dev)
+    ws = WeightSet(torch.from_numpy(ins["b"]).to(dev), torch.from_numpy(ins["bias"]).to(dev))
+    out = torch.full((m, n), float("nan"), device=dev)
+    for r0, r1 in all_partitions(m, 3):
+        mbr_rows(A[r0:r1], ws, out[r0:r1], "fp32")
+    torch.cuda.synchronize()
+    res = tc.check_output("mbr", ins, out.cpu().numpy(), "fp32")
+    assert res["pass"] and res["nan_count"] == 0, res
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16", "tf32"])
+def test_mlp_chain_per_layer_bound(gpu, mode):
+    """relu(relu(X W1 + b1) W2 + b2), Xavier weights, N(0, 0.02) biases; each layer checked
+    against FP64 with its own bound (layer 2 on the kernel's own H)."""
+    import torch
+    from tensorforge_b200.mlp import MLP2
+
+    ins = tc.make_mlp_inputs(640, 256, 1024, seed=3)
+    dev = torch.device("cuda", 0)
+    t = {k: torch.from_numpy(v).to(dev) for k, v in ins.items()}
+    model = MLP2(t["w1"], t["b1"], t["w2"], t["b2"], mode)
+    h, out = model(t["x"])
+    torch.cuda.synchronize()
+    assert _lib.device_status(None) == 0
+    hn, on = h.cpu().numpy(), out.cpu().numpy()
+    r1 = tc.check_output("mbr", {"a": ins["x"], "b": ins["w1"], "bias": ins["b1"]}, hn, mode)
+    r2 = tc.check_output("mbr", {"a": hn, "b": ins["w2"], "bias": ins["b2"]}, on, mode)
+    assert r1["pass"] and r2["pass"], (r1, r2)
