@@ -14,6 +14,7 @@ What it records, and from where:
 * ``reference_check``: the reference's own ``tforge_cpu.check`` (FP64 bound), driving the
   reference's own CPU harness (runners/cpu/tforge-cpu-bench.cpp, built by
   ``make -C oracle ref``) with the CPU restatement ``oracle/build/k_<workload>.so``.
+* ``provenance_fields``: the reference's CSV schema (python/provenance.py:11-16).
 * ``outputs``: sha256 of the harness's output bytes for small cases, plus the full
   output of a tiny case, so CPU tests can check the restatement without the reference.
 
@@ -111,6 +112,10 @@ def main() -> int:
         if m * n <= 200:
             entry["values_hex"] = [format(int(v), "08x") for v in out.view(np.uint32).ravel()]
         golden["outputs"].append(entry)
+
+    import provenance as rprov  # the reference's CSV schema (python/provenance.py:11-16)
+
+    golden["provenance_fields"] = list(rprov.FIELDS)
 
     (HERE / "golden.json").write_text(json.dumps(golden, indent=1) + "\n")
     print("wrote", HERE / "golden.json")

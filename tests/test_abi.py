@@ -139,3 +139,20 @@ def test_tensor_roofline_from_measured_peaks():
     assert tg.tensor_roofline_tflops("tf32", peaks)[0] == 800.0
     assert tg.tensor_roofline_tflops("fp32", peaks)[0] == pytest.approx(800.0 / 3)
     assert tg.tensor_roofline_tflops("fp32", {})[1] == "of fallback"
+
+
+def test_csv_schema_is_the_references(tmp_path):
+    import csv
+    import json
+
+    from tensorforge_b200 import provenance
+
+    golden = json.loads((REPO / "tests" / "golden" / "golden.json").read_text())
+    assert provenance.FIELDS == golden["provenance_fields"]
+    w = provenance.CsvWriter(tmp_path / "r.csv")
+    w.row(**provenance.common(), workload="mbr", shape="2x2x2")
+    with pytest.raises(KeyError):
+        w.row(bogus=1)
+    w.close()
+    rows = list(csv.DictReader(open(tmp_path / "r.csv")))
+    assert rows[0]["workload"] == "mbr" and list(rows[0]) == provenance.FIELDS
