@@ -280,8 +280,20 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   p.limit_ns = g_wait_limit_ns.load();
   p.debug_skip = g_debug_skip.load();
   const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
-  cudaError_t e = cfg.pair ? launch_gemm_pair(cfg.prec, cfg.stages, epi, tmA, tmB, p, st)
-                           : launch_gemm_tc(cfg, epi, tmA, tmB, p, st);
+  cudaError_t e;
+  if (cfg.pair) {
+    CUtensorMap tmO, tmC;
+    rc = make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 32, 128);
+    if (rc) return rc;
+    tmC = tmO;
+    if (a->workload == TFORGE_MATMUL_ADD) {
+      rc = make_tmap(&tmC, a->C_res, false, a->M, a->N, ldc, 32, 128);
+      if (rc) return rc;
+    }
+    e = launch_gemm_pair(cfg.prec, cfg.stages, epi, tmA, tmB, tmO, tmC, p, st);
+  } else {
+    e = launch_gemm_tc(cfg, epi, tmA, tmB, p, st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
   return TFORGE_OK;
 }

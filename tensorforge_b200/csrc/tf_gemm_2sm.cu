@@ -66,7 +66,7 @@ struct PairLayout {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kLoBytes = PREC == PREC_X3 ? kBBytes : 0;  // B lo (A lo lives in TMEM)
   static constexpr int kRingBytes = STAGES * (kStageBytes + kLoBytes);
-  static constexpr int kNumBars = 4 * STAGES + 1;      // full, conv, ready, empty, accf
+  static constexpr int kNumBars = 4 * STAGES + 2;      // full, conv, ready, empty, accf, resf
   static constexpr int kBarBytes = 8 * kNumBars + 16;
   static constexpr int kSmemBytes = 1024 + kRingBytes + kBarBytes;
   static constexpr uint32_t kAccCols = 256;
@@ -78,6 +78,9 @@ struct PairLayout {
   __host__ __device__ static constexpr int bar_off() { return kRingBytes; }
   __host__ __device__ static constexpr uint32_t a_tmem_col(int s) { return kAccCols + 64u * s; }
   static_assert(PREC != PREC_X3 || kAccCols + 64u * STAGES <= 512u, "TMEM budget");
+  // Epilogue staging: eight 128-row x 32-column f32 boxes (16 KB each) reuse the ring.
+  static constexpr int kEpiBoxBytes = 128 * 128;
+  static_assert(8 * kEpiBoxBytes <= kRingBytes, "epilogue staging fits in the ring");
 };
 
 // Bounded pause (abort drains of loads this CTA cannot observe).
@@ -89,6 +92,7 @@ __device__ __forceinline__ void pause_ns(uint64_t ns) {
 template <int PREC, int STAGES, int EPI, int SPLIT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STAGES>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmC,
                      const TcParams p) {
   using L = PairLayout<PREC, STAGES>;
   constexpr bool kX3 = PREC == PREC_X3;
@@ -104,7 +108,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   // both CTAs' bytes); conv[s]: this CTA's converters done; ready[s] (leader): the peer's
   // converters done; empty[s]: the pair MMAs reading stage s done; accf: accumulator done.
   const uint32_t full0 = smem_u32(bars), conv0 = full0 + 8 * STAGES, ready0 = conv0 + 8 * STAGES,
-                 empty0 = ready0 + 8 * STAGES, accf = empty0 + 8 * STAGES;
+                 empty0 = ready0 + 8 * STAGES, accf = empty0 + 8 * STAGES, resf = accf + 8;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
@@ -122,10 +126,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(accf, 1);
+    mbar_init(resf, 1);
     *abort_flag = 0u;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
+    if constexpr (EPI == EPI_ADD) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
@@ -289,48 +296,79 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
     }
   }
 
-  // ---------------- epilogue: TMEM -> registers -> global (both CTAs) ----------------
+  // ---------------- epilogue: TMEM -> registers -> smem -> TMA store (both CTAs) ----------------
+  // Column chunk c (32 columns) of this CTA's 128 rows: the warp of TMEM lane quadrant q
+  // takes rows 32 q .. +31, applies the epilogue and writes them into staging box c
+  // (128-B swizzle: 16-B unit j of row r at unit j ^ (r % 8), matching the output tensor
+  // map); after the four quadrant warps of chunk c meet at named barrier 1 + c, one thread
+  // stores the box with TMA, which clips rows >= M and columns >= N.  The ring is free:
+  // every load was consumed before accf.  matmul_add first brings its C_res boxes in the
+  // same way (TMA loads into the boxes, then in-place update).
   if (warp >= 4) {
-    if (mbar_wait_cluster(accf, 0, wc, 128)) {
+    // One thread waits (bounded) for the accumulator and publishes the outcome, so every
+    // epilogue warp takes the same branch and the named barriers below cannot be left
+    // waiting for a warp that gave up.
+    constexpr int kEpiThreads = L::kThreads - 128;
+    volatile uint32_t *epi_ok = tmem_slot + 2;
+    if (warp == 4 && lane == 0) *epi_ok = mbar_wait_cluster(accf, 0, wc, 128) ? 1u : 0u;
+    named_barrier(9, kEpiThreads);
+    if (*epi_ok) {
       tc_fence_after();
-      const int q = warp & 3;
       constexpr int kEpiWarps = L::kThreads / 32 - 4;     // 4 or 8
       constexpr int kChunksPerWarp = 8 / (kEpiWarps / 4);  // column chunks of 32 per warp
+      const int q = warp & 3;
       const int c0 = ((warp - 4) >> 2) * kChunksPerWarp;
-      const int row = m0 + q * 32 + lane;
-      const bool row_ok = row < p.M;
-      float *orow = p.out + (int64_t)row * p.ldc;
+      const int r = q * 32 + lane;  // row within this CTA's 128 rows
+      const bool cta_rows = m0 < p.M;
+      bool res_ok = true;
+      if constexpr (EPI == EPI_ADD) {
+        if (warp == 4 && lane == 0 && cta_rows) {
+          mbar_arrive_expect_tx(resf, 8 * L::kEpiBoxBytes);
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c)
+            tma_load_2d(sbase + c * L::kEpiBoxBytes, &tmC, n0 + c * 32, m0, resf);
+        }
+        res_ok = !cta_rows || mbar_wait_cluster(resf, 0, wc);
+      }
 #pragma unroll 1
       for (int c = c0; c < c0 + kChunksPerWarp; ++c) {
         uint32_t rr[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, rr);
         tmem_ld_wait();
         const int col0 = n0 + c * 32;
-        if (row_ok && col0 < p.N) {
+        uint8_t *box = smem + c * L::kEpiBoxBytes + r * 128;
+        if (res_ok && cta_rows && col0 < p.N) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const int col = col0 + j;
-            if (col < p.N) {
-              float4 v = make_float4(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]),
-                                     __uint_as_float(rr[j + 2]), __uint_as_float(rr[j + 3]));
-              if constexpr (EPI == EPI_MBR) {
-                const float4 b = __ldg(reinterpret_cast<const float4 *>(p.bias + col));
-                v.x = relu_ieee(__fadd_rn(v.x, b.x));
-                v.y = relu_ieee(__fadd_rn(v.y, b.y));
-                v.z = relu_ieee(__fadd_rn(v.z, b.z));
-                v.w = relu_ieee(__fadd_rn(v.w, b.w));
-              } else if constexpr (EPI == EPI_ADD) {
-                const float4 cr = __ldg(reinterpret_cast<const float4 *>(p.cres + (int64_t)row * p.ldc + col));
-                v.x = __fadd_rn(v.x, cr.x);
-                v.y = __fadd_rn(v.y, cr.y);
-                v.z = __fadd_rn(v.z, cr.z);
-                v.w = __fadd_rn(v.w, cr.w);
-              }
-              *reinterpret_cast<float4 *>(orow + col) = v;
+          for (int j = 0; j < 8; ++j) {
+            float4 v = make_float4(__uint_as_float(rr[4 * j]), __uint_as_float(rr[4 * j + 1]),
+                                   __uint_as_float(rr[4 * j + 2]), __uint_as_float(rr[4 * j + 3]));
+            float4 *slot = reinterpret_cast<float4 *>(box + ((j ^ (r & 7)) << 4));
+            if constexpr (EPI == EPI_MBR) {
+              const int col = col0 + 4 * j;
+              const float4 b = col < p.N ? __ldg(reinterpret_cast<const float4 *>(p.bias + col))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+              v.x = relu_ieee(__fadd_rn(v.x, b.x));
+              v.y = relu_ieee(__fadd_rn(v.y, b.y));
+              v.z = relu_ieee(__fadd_rn(v.z, b.z));
+              v.w = relu_ieee(__fadd_rn(v.w, b.w));
+            } else if constexpr (EPI == EPI_ADD) {
+              const float4 cr = *slot;
+              v.x = __fadd_rn(v.x, cr.x);
+              v.y = __fadd_rn(v.y, cr.y);
+              v.z = __fadd_rn(v.z, cr.z);
+              v.w = __fadd_rn(v.w, cr.w);
             }
+            *slot = v;
           }
         }
+        fence_proxy_async_smem();
+        named_barrier(1 + c, 128);
+        if (q == 0 && lane == 0 && res_ok && cta_rows && col0 < p.N) {
+          tma_store_2d(&tmO, sbase + c * L::kEpiBoxBytes, col0, m0);
+          bulk_commit_group();
+        }
       }
+      if (q == 0 && lane == 0) bulk_wait_group_read0();  // staging stays valid until read
     }
   }
 
@@ -344,8 +382,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
 }
 
 template <int PREC, int STAGES, int EPI>
-cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
-                            cudaStream_t stream) {
+cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
+                            const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   using L = PairLayout<PREC, STAGES>;
   auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit>;
   static unsigned long long configured = 0;
@@ -358,17 +396,17 @@ cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, cons
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
   dim3 grid(2 * ((p.N + 255) / 256), (p.M + 255) / 256, 1);
-  kern<<<grid, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, p);
+  kern<<<grid, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, tmO, tmC, p);
   return cudaGetLastError();
 }
 
 template <int PREC, int STAGES>
-cudaError_t launch_pair_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
-                            cudaStream_t stream) {
+cudaError_t launch_pair_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
+                            const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   switch (epi) {
-    case EPI_MATMUL: return launch_pair_one<PREC, STAGES, EPI_MATMUL>(tmA, tmB, p, stream);
-    case EPI_MBR: return launch_pair_one<PREC, STAGES, EPI_MBR>(tmA, tmB, p, stream);
-    case EPI_ADD: return launch_pair_one<PREC, STAGES, EPI_ADD>(tmA, tmB, p, stream);
+    case EPI_MATMUL: return launch_pair_one<PREC, STAGES, EPI_MATMUL>(tmA, tmB, tmO, tmC, p, stream);
+    case EPI_MBR: return launch_pair_one<PREC, STAGES, EPI_MBR>(tmA, tmB, tmO, tmC, p, stream);
+    case EPI_ADD: return launch_pair_one<PREC, STAGES, EPI_ADD>(tmA, tmB, tmO, tmC, p, stream);
   }
   return cudaErrorInvalidValue;
 }
@@ -402,9 +440,10 @@ int pair_smem_bytes(int prec, int stages) {
 int pair_tmem_cols(int prec) { return prec == PREC_X3 ? 512 : 256; }
 
 cudaError_t launch_gemm_pair(int prec, int stages, int epi, const CUtensorMap &tmA,
-                             const CUtensorMap &tmB, const TcParams &p, cudaStream_t stream) {
+                             const CUtensorMap &tmB, const CUtensorMap &tmO, const CUtensorMap &tmC,
+                             const TcParams &p, cudaStream_t stream) {
 #define TF_PLAUNCH(P, S) \
-  if (prec == P && stages == S) return launch_pair_epi<P, S>(epi, tmA, tmB, p, stream);
+  if (prec == P && stages == S) return launch_pair_epi<P, S>(epi, tmA, tmB, tmO, tmC, p, stream);
   TF_PAIR_CONFIGS(TF_PLAUNCH)
 #undef TF_PLAUNCH
   return cudaErrorInvalidValue;

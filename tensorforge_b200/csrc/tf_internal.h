@@ -47,8 +47,11 @@ cudaError_t simt_func_attributes(int epi, cudaFuncAttributes *attr, int *blocks_
 // CTA-pair (cta_group::2) kernel: 256 x 256 output tiles, clusters of two CTAs.
 int pair_smem_bytes(int prec, int stages);
 int pair_tmem_cols(int prec);
+// tmO / tmC: f32 maps of the output and of C_res (box 32 columns x 128 rows, 128-B
+// swizzle) for the TMA-store epilogue; tmC is read only by matmul_add.
 cudaError_t launch_gemm_pair(int prec, int stages, int epi, const CUtensorMap &tmA,
-                             const CUtensorMap &tmB, const TcParams &p, cudaStream_t stream);
+                             const CUtensorMap &tmB, const CUtensorMap &tmO, const CUtensorMap &tmC,
+                             const TcParams &p, cudaStream_t stream);
 cudaError_t pair_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *attr,
                                  int *blocks_per_sm);
 

@@ -127,8 +127,14 @@ extern "C" int tforge_mbr_bf16_noalloc(const float *A, const float *B, const flo
   p.status = status;
   p.limit_ns = 1000000000ull;
   p.debug_skip = 0;
-  e = cfg.pair ? tf::launch_gemm_pair(cfg.prec, cfg.stages, tf::EPI_MBR, tmA, tmB, p, st)
-               : tf::launch_gemm_tc(cfg, tf::EPI_MBR, tmA, tmB, p, st);
+  if (cfg.pair) {
+    CUtensorMap tmO;
+    rc = tf::encode_operand_map(&tmO, out, false, M, N, N, 32, 128, false);
+    if (rc) return rc;
+    e = tf::launch_gemm_pair(cfg.prec, cfg.stages, tf::EPI_MBR, tmA, tmB, tmO, tmO, p, st);
+  } else {
+    e = tf::launch_gemm_tc(cfg, tf::EPI_MBR, tmA, tmB, p, st);
+  }
   if (e != cudaSuccess) {
     tf::set_last_error(cudaGetErrorString(e));
     return TFORGE_ERR_CUDA;

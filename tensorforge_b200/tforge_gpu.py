@@ -78,7 +78,17 @@ def run(cmd, **kw):
 def parse_options(options: str) -> dict:
     opts = dict(o.split("=", 1) for o in options.split() if "=" in o)
     return {"precision": opts.get("precision", "fp32"), "bn": int(opts.get("bn", 0)),
-            "stages": int(opts.get("stages", 0))}
+            "stages": int(opts.get("stages", 0)), "kernel": opts.get("kernel", "")}
+
+
+def _forced_kind(o: dict) -> int:
+    """tforge_config.kernel for parsed options: 0 table, 1 one-CTA, 2 SIMT, 3 CTA pair."""
+    k = o.get("kernel", "")
+    if k == "pair":
+        return 3
+    if k == "simt":
+        return 2
+    return 1 if (k == "cta" or o["bn"] or o["stages"]) else 0
 
 
 def padded_shape(m, n, k, options=""):
@@ -95,12 +105,13 @@ def compile_kernel(workload, m, n, k, options="", tag="default"):
     o = parse_options(options)
     d = ART / tag / f"{workload}_{m}x{n}x{k}"
     d.mkdir(parents=True, exist_ok=True)
-    if o["bn"] or o["stages"]:
-        _lib.set_config(1, o["bn"], o["stages"])
+    kind = _forced_kind(o)
+    if kind:
+        _lib.set_config(kind, o["bn"], o["stages"])
     try:
         desc = _lib.describe(workload, m, n, k or 0, o["precision"])
     finally:
-        if o["bn"] or o["stages"]:
+        if kind:
             _lib.set_config()
     args = {"matmul": ["arg0", "arg1", "arg2"], "mbr": ["arg0", "arg1", "arg2", "arg3"],
             "matmul_add": ["arg0", "arg1", "arg2", "arg3"], "bias_add": ["arg0", "arg1", "arg2"],
@@ -123,6 +134,8 @@ def _bench_cmd(workload, m, n, k, kdir=None, launch=None, mode="kernel"):
             cmd += ["--bn", o["bn"]]
         if o["stages"]:
             cmd += ["--stages", o["stages"]]
+        if o["kernel"]:
+            cmd += ["--kernel", o["kernel"]]
     return cmd
 
 
@@ -176,8 +189,9 @@ def run_op(workload: str, ins: dict, m: int, n: int, k: int | None, precision: s
     out = DeviceBuffer(m * n * 4)
     _lib.check(L.tforge_memset(out.ptr, 0xFF, m * n * 4, None), "memset")  # NaN prefill
     o = parse_options(options)
-    if o["bn"] or o["stages"]:
-        _lib.set_config(1, o["bn"], o["stages"])
+    kind = _forced_kind(o)
+    if kind:
+        _lib.set_config(kind, o["bn"], o["stages"])
     try:
         if workload in tc.GEMM_WORKLOADS:
             _lib.gemm(workload, bufs["a"].addr, bufs["b"].addr, out.addr, m, n, k, precision,
@@ -194,7 +208,7 @@ def run_op(workload: str, ins: dict, m: int, n: int, k: int | None, precision: s
         _lib.check(_lib.device_status(None), "device status")
         return out.download((m, n))
     finally:
-        if o["bn"] or o["stages"]:
+        if kind:
             _lib.set_config()
         for b in bufs.values():
             b.free()
