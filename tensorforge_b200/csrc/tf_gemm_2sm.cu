@@ -51,7 +51,9 @@ namespace {
 
 template <int PREC, int STAGES>
 struct PairLayout {
+  // 3xTF32: warps 0 producer, 1 MMA (leader) / relay (peer), 2..11 converters.
   static constexpr int kThreads = PREC == PREC_X3 ? 384 : 256;
+  static constexpr int kEpiWarps = PREC == PREC_X3 ? 8 : 4;  // warps 4 .. 4 + kEpiWarps - 1
   static constexpr int kElem = PREC == PREC_BF16 ? 2 : 4;
   static constexpr int kBK = 128 / kElem;              // K elements per stage (one 128-B row)
   static constexpr int kUmmaK = 32 / kElem;            // K per MMA instruction
@@ -67,7 +69,9 @@ struct PairLayout {
   static constexpr int kLoBytes = PREC == PREC_X3 ? kBBytes : 0;  // B lo (A lo lives in TMEM)
   static constexpr int kRingBytes = STAGES * (kStageBytes + kLoBytes);
   static constexpr int kNumBars = 4 * STAGES + 2;      // full, conv, ready, empty, accf, resf
-  static constexpr int kBarBytes = 8 * kNumBars + 16;
+  // barriers, then tmem slot, abort flag, epilogue flag, spare, and one mailbox word per
+  // stage (the peer's st.async tokens land there).
+  static constexpr int kBarBytes = 8 * kNumBars + 16 + 4 * STAGES;
   static constexpr int kSmemBytes = 1024 + kRingBytes + kBarBytes;
   static constexpr uint32_t kAccCols = 256;
   static constexpr uint32_t kTmemCols = PREC == PREC_X3 ? 512u : 256u;
@@ -87,6 +91,20 @@ struct PairLayout {
 __device__ __forceinline__ void pause_ns(uint64_t ns) {
   const uint64_t t0 = globaltimer();
   while (globaltimer() - t0 < ns) __nanosleep(1000);
+}
+
+// Peer CTA of a 3xTF32 pair: forwards "this CTA's converters finished stage kb" (local
+// conv[s]) to the leader: an st.async of a 4-byte token into the leader's mailbox word for
+// stage s completes the leader's ready[s] (which its MMA thread armed with expect_tx(4)).
+template <int STAGES>
+__device__ __forceinline__ void relay_stages(uint32_t conv0, uint32_t ready0, uint32_t mailbox0, int nkb,
+                                             const WaitCtl &wc) {
+  const uint32_t lead_ready0 = map_to_cta(ready0, 0), lead_mail0 = map_to_cta(mailbox0, 0);
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int s = kb % STAGES, round = kb / STAGES;
+    if (!mbar_wait(conv0 + 8 * s, round & 1, wc)) break;
+    st_async_signal(lead_mail0 + 4 * s, (uint32_t)kb, lead_ready0 + 8 * s);
+  }
 }
 
 template <int PREC, int STAGES, int EPI, int SPLIT>
@@ -111,6 +129,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
                  empty0 = ready0 + 8 * STAGES, accf = empty0 + 8 * STAGES, resf = accf + 8;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile uint32_t *abort_flag = tmem_slot + 1;
+  const uint32_t mailbox0 = smem_u32(tmem_slot + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -192,6 +211,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         const int s = kb % STAGES, round = kb / STAGES;
         if constexpr (kX3) {
           if (!mbar_wait(conv0 + 8 * s, round & 1, wc)) break;
+          mbar_arrive_expect_tx(ready0 + 8 * s, 4);  // the peer's token for this round
           if (!mbar_wait_cluster(ready0 + 8 * s, round & 1, wc)) break;
         } else {
           if (!mbar_wait_cluster(full0 + 8 * s, round & 1, wc)) break;
@@ -219,13 +239,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       mma_commit_pair(accf, 0x3);
       if (*abort_flag) mbar_wait_drain_cluster(accf, 0, p.limit_ns);
     } else if constexpr (kX3) {
-      // ---------------- relay (peer CTA): conv[s] -> leader's ready[s] ----------------
-      const uint32_t lead_ready0 = map_to_cta(ready0, 0);
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
-        if (!mbar_wait(conv0 + 8 * s, round & 1, wc)) break;
-        mbar_arrive_cluster(lead_ready0 + 8 * s);
-      }
+      relay_stages<STAGES>(conv0, ready0, mailbox0, nkb, wc);
     }
   } else if (kX3 && warp >= 2) {
     // ---------------- 3xTF32 converters (both CTAs, warps 2..11) ----------------
@@ -237,58 +251,96 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       if (!mbar_wait(full0 + 8 * s, round & 1, wc)) break;
       float4 *braw = reinterpret_cast<float4 *>(smem + L::b_off(s));
       float4 *blo = reinterpret_cast<float4 *>(smem + L::lo_off(s));
+      // Row r of the A tile: 128 B at r * 128, 16-B chunk j stored at j ^ (r % 8); warps
+      // 4..11 split K elements [16 h, 16 h + 16) of their row into TMEM columns of stage s.
+      const uint8_t *arow = smem + L::a_off(s) + r * 128;
+      if constexpr (SPLIT == 1) {
+        // All shared-memory loads of this thread first (B: chunks t + 320 i; A: 4 chunks),
+        // then the 2-op truncation split, so the warp keeps several loads in flight.
+        float4 xb[4], xa[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (t + 320 * i < kChunks) xb[i] = braw[t + 320 * i];
+        if (warp >= 4) {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+            xa[jj] = *reinterpret_cast<const float4 *>(arow + (((4 * h + jj) ^ (r & 7)) << 4));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = t + 320 * i;
+          if (c < kChunks) {
+            bool special;
+            blo[c] = split_lo_trunc4(xb[i], special);
+            if (special) {  // a non-finite element (rare): exact per-element handling
+              blo[c] = make_float4(split_lo_trunc(xb[i].x), split_lo_trunc(xb[i].y),
+                                   split_lo_trunc(xb[i].z), split_lo_trunc(xb[i].w));
+              braw[c] = make_float4(__uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].x))),
+                                    __uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].y))),
+                                    __uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].z))),
+                                    __uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].w))));
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        if (warp >= 4) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            bool special;
+            const float4 l = split_lo_trunc4(xa[jj], special);
+            const float xs[4] = {xa[jj].x, xa[jj].y, xa[jj].z, xa[jj].w};
+            const float ls[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              hi[4 * jj + i] = __float_as_uint(xs[i]);
+              lo[4 * jj + i] = __float_as_uint(ls[i]);
+            }
+            if (special) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                hi[4 * jj + i] = split_hi_trunc_bits(__float_as_uint(xs[i]));
+                lo[4 * jj + i] = __float_as_uint(split_lo_trunc(xs[i]));
+              }
+            }
+          }
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + L::a_tmem_col(s) + 16 * h;
+          tmem_st_32x32b_x16(ta, hi);
+          tmem_st_32x32b_x16(ta + 32, lo);
+          tmem_st_wait();
+        }
+      } else {
 #pragma unroll 2
-      for (int c = t; c < kChunks; c += 320) {
-        const float4 x = braw[c];
-        float4 l;
-        if constexpr (SPLIT == 1) {
-          l.x = split_lo_trunc(x.x); l.y = split_lo_trunc(x.y);
-          l.z = split_lo_trunc(x.z); l.w = split_lo_trunc(x.w);
-          const uint4 u = make_uint4(__float_as_uint(x.x), __float_as_uint(x.y), __float_as_uint(x.z),
-                                     __float_as_uint(x.w));
-          const uint4 hu = make_uint4(split_hi_trunc_bits(u.x), split_hi_trunc_bits(u.y),
-                                      split_hi_trunc_bits(u.z), split_hi_trunc_bits(u.w));
-          if ((hu.x ^ u.x) | (hu.y ^ u.y) | (hu.z ^ u.z) | (hu.w ^ u.w))  // a NaN to quiet (rare)
-            braw[c] = make_float4(__uint_as_float(hu.x), __uint_as_float(hu.y), __uint_as_float(hu.z),
-                                  __uint_as_float(hu.w));
-        } else {
-          float4 hh;
+        for (int c = t; c < kChunks; c += 320) {
+          const float4 x = braw[c];
+          float4 hh, l;
           hh.x = to_tf32(x.x); hh.y = to_tf32(x.y); hh.z = to_tf32(x.z); hh.w = to_tf32(x.w);
           l.x = isfinite(hh.x) ? to_tf32(x.x - hh.x) : 0.f;
           l.y = isfinite(hh.y) ? to_tf32(x.y - hh.y) : 0.f;
           l.z = isfinite(hh.z) ? to_tf32(x.z - hh.z) : 0.f;
           l.w = isfinite(hh.w) ? to_tf32(x.w - hh.w) : 0.f;
           braw[c] = hh;
+          blo[c] = l;
         }
-        blo[c] = l;
-      }
-      fence_proxy_async_smem();
-      if (warp >= 4) {
-        // Row r of the A tile (128 B at r * 128, 16-B chunk j stored at j ^ (r % 8)); this
-        // warp splits K elements [16 h, 16 h + 16) into TMEM columns of stage s.
-        const uint8_t *arow = smem + L::a_off(s) + r * 128;
-        uint32_t hi[16], lo[16];
+        fence_proxy_async_smem();
+        if (warp >= 4) {
+          uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = 4 * h + jj;
-          const float4 v = *reinterpret_cast<const float4 *>(arow + ((j ^ (r & 7)) << 4));
-          const float xs[4] = {v.x, v.y, v.z, v.w};
+          for (int jj = 0; jj < 4; ++jj) {
+            const float4 v = *reinterpret_cast<const float4 *>(arow + (((4 * h + jj) ^ (r & 7)) << 4));
+            const float xs[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if constexpr (SPLIT == 1) {
-              hi[4 * jj + i] = split_hi_trunc_bits(__float_as_uint(xs[i]));
-              lo[4 * jj + i] = __float_as_uint(split_lo_trunc(xs[i]));
-            } else {
+            for (int i = 0; i < 4; ++i) {
               const float hv = to_tf32(xs[i]);
               hi[4 * jj + i] = __float_as_uint(hv);
               lo[4 * jj + i] = __float_as_uint(isfinite(hv) ? to_tf32(xs[i] - hv) : 0.f);
             }
           }
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + L::a_tmem_col(s) + 16 * h;
+          tmem_st_32x32b_x16(ta, hi);
+          tmem_st_32x32b_x16(ta + 32, lo);
+          tmem_st_wait();
         }
-        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + L::a_tmem_col(s) + 16 * h;
-        tmem_st_32x32b_x16(ta, hi);
-        tmem_st_32x32b_x16(ta + 32, lo);
-        tmem_st_wait();
       }
       tc_fence_before();
       __syncwarp();
@@ -304,18 +356,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   // stores the box with TMA, which clips rows >= M and columns >= N.  The ring is free:
   // every load was consumed before accf.  matmul_add first brings its C_res boxes in the
   // same way (TMA loads into the boxes, then in-place update).
-  if (warp >= 4) {
+  if (warp >= 4 && warp < 4 + L::kEpiWarps) {
     // One thread waits (bounded) for the accumulator and publishes the outcome, so every
     // epilogue warp takes the same branch and the named barriers below cannot be left
     // waiting for a warp that gave up.
-    constexpr int kEpiThreads = L::kThreads - 128;
+    constexpr int kEpiThreads = 32 * L::kEpiWarps;
     volatile uint32_t *epi_ok = tmem_slot + 2;
     if (warp == 4 && lane == 0) *epi_ok = mbar_wait_cluster(accf, 0, wc, 128) ? 1u : 0u;
     named_barrier(9, kEpiThreads);
     if (*epi_ok) {
       tc_fence_after();
-      constexpr int kEpiWarps = L::kThreads / 32 - 4;     // 4 or 8
-      constexpr int kChunksPerWarp = 8 / (kEpiWarps / 4);  // column chunks of 32 per warp
+      constexpr int kChunksPerWarp = 8 / (L::kEpiWarps / 4);  // column chunks of 32 per warp
       const int q = warp & 3;
       const int c0 = ((warp - 4) >> 2) * kChunksPerWarp;
       const int r = q * 32 + lane;  // row within this CTA's 128 rows

@@ -219,6 +219,17 @@ __device__ __forceinline__ uint32_t map_to_cta(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Non-blocking 4-byte store into another CTA's shared memory whose completion performs
+// complete_tx(4) on that CTA's mbarrier; the complete-tx has release semantics at cluster
+// scope, so it publishes this thread's prior writes (and those it acquired) to a waiter
+// that acquires the barrier, without stalling the issuing thread the way a fenced
+// remote arrive does.
+__device__ __forceinline__ void st_async_signal(uint32_t remote_word, uint32_t value, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.u32 [%0], %1, [%2];" ::"r"(remote_word),
+               "r"(value), "r"(remote_bar)
+               : "memory");
+}
+
 // try_wait with acquire at cluster scope (barriers that peers or pair commits arrive on).
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -372,6 +383,18 @@ __device__ __forceinline__ float relu_ieee(float x) {
 __device__ __forceinline__ float split_lo_trunc(float x) {
   const uint32_t u = __float_as_uint(x);
   return ((u & 0x7F800000u) == 0x7F800000u) ? 0.0f : __fsub_rn(x, __uint_as_float(u & 0xFFFFE000u));
+}
+// Truncation split of four elements on the fast path (2 ops each); `special` reports a
+// non-finite element (exponent all ones), which the caller redoes element by element.
+__device__ __forceinline__ float4 split_lo_trunc4(const float4 x, bool &special) {
+  const uint32_t ux = __float_as_uint(x.x), uy = __float_as_uint(x.y), uz = __float_as_uint(x.z),
+                 uw = __float_as_uint(x.w);
+  constexpr uint32_t kExp = 0x7F800000u;
+  special = max(max(ux & kExp, uy & kExp), max(uz & kExp, uw & kExp)) == kExp;
+  return make_float4(__fsub_rn(x.x, __uint_as_float(ux & 0xFFFFE000u)),
+                     __fsub_rn(x.y, __uint_as_float(uy & 0xFFFFE000u)),
+                     __fsub_rn(x.z, __uint_as_float(uz & 0xFFFFE000u)),
+                     __fsub_rn(x.w, __uint_as_float(uw & 0xFFFFE000u)));
 }
 __device__ __forceinline__ uint32_t split_hi_trunc_bits(uint32_t u) {
   return ((u & 0x7FFFFFFFu) > 0x7F800000u) ? (u | 0x00400000u) : u;
