@@ -21,8 +21,8 @@ reference's convention, python/tforge_cpu.py:154-157).
 Also reported: `roofline` of the GEMM kernel against the measured bf16 peak scaled to the
 mode (TF32 = bf16 / 2, 3xTF32 = TF32 / 3); `cpu_baseline` (the CPU restatement of the
 reference kernel, pinned to the reference's published numerics, timed on the host cores
-over row slices); `e2e` through the C-ABI with pinned host buffers and the copies in the
-timed region; `clocks` sampled through NVML during the timed region.
+over row slices); `e2e` through the C-ABI's host-buffer entry (tforge_gemm_host) on pinned
+host buffers, with the chunked, overlapped copies in the timed region; `clocks` sampled through NVML during the timed region.
 
 `--impl reference` times the reference's own CPU implementation of the path (its MLIR
 pipeline cannot be built here, so the pinned C restatement stands in) on all host
@@ -441,24 +441,22 @@ def cublas_comparator(m, n, k, A, B, bias, flush, stream):
 
 
 def e2e_measure(L, _lib, m, n, k, mode, A, B, bias, world, dev, steps=20, warmup=3):
-    """The same operator through the C-ABI on HOST buffers: pinned H2D of A, B and bias, the
-    fused kernel, D2H of the output, all inside the timed region (CUDA events)."""
+    """The same operator through the C-ABI on HOST buffers (tforge_gemm_host): A, B and bias
+    in page-locked host memory are copied in, the fused kernel runs per row chunk as the
+    chunk lands, and out is copied back per chunk, all inside the timed region (CUDA events
+    on the caller's stream, which the call joins)."""
     import torch
 
     hA, hB, hb = A.cpu().pin_memory(), B.cpu().pin_memory(), bias.cpu().pin_memory()
     hO = torch.empty((m, n), dtype=torch.float32).pin_memory()
-    dA, dB, db, dO = torch.empty_like(A), torch.empty_like(B), torch.empty_like(bias), torch.empty((m, n), device=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     h2d = hA.numel() * 4 + hB.numel() * 4 + hb.numel() * 4
     d2h = hO.numel() * 4
 
     def one():
-        for dst, src, nb in ((dA, hA, hA.numel() * 4), (dB, hB, hB.numel() * 4), (db, hb, hb.numel() * 4)):
-            _lib.check(L.tforge_memcpy_h2d(dst.data_ptr(), src.data_ptr(), nb, sp), "H2D")
-        _lib.check(L.tforge_mbr(dA.data_ptr(), dB.data_ptr(), db.data_ptr(), dO.data_ptr(), m, n, k,
-                                _lib.MODES[mode], sp), "tforge_mbr")
-        _lib.check(L.tforge_memcpy_d2h(hO.data_ptr(), dO.data_ptr(), d2h, sp), "D2H")
+        _lib.gemm_host("mbr", hA.data_ptr(), hB.data_ptr(), hO.data_ptr(), m, n, k, mode,
+                       bias=hb.data_ptr(), stream=sp)
 
     for _ in range(warmup):
         one()
@@ -472,7 +470,9 @@ def e2e_measure(L, _lib, m, n, k, mode, A, B, bias, world, dev, steps=20, warmup
     ms = e0.elapsed_time(e1) / steps
     return {"value": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms, "steps": steps,
-            "path": "tforge_memcpy_h2d x3 -> tforge_mbr -> tforge_memcpy_d2h (pinned host buffers), rank 0"}
+            "h2d_plus_d2h_gbs": (h2d + d2h) / (ms * 1e-3) / 1e9,
+            "path": "tforge_gemm_host (pinned host A, B, bias, out; B first, A in row chunks, "
+                    "per-chunk kernels and copy-back overlapped), rank 0"}
 
 
 def main():

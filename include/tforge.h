@@ -89,6 +89,18 @@ typedef struct tforge_gemm_args {
 
 int tforge_gemm(const tforge_gemm_args *args, void *stream);
 
+/* tforge_gemm on HOST buffers: args->A, B, bias / C_res and out are host pointers (pitches as in
+ * tforge_gemm).  Replaces the GPU runner's host flow -- cudaMalloc, cudaMemcpy of A, B and bias
+ * to the device, the launch, cudaMemcpy of C back (runners/gpu/tforge-gpu-bench.cu:198-207,
+ * 292-302,327) -- with an overlapped one: device staging comes from the library's pool; B and
+ * bias are copied first, then A (and C_res) in chunks of `chunk_rows` rows (0: automatic, at
+ * most 8 chunks); each chunk's kernel starts on its own stream once its rows have landed,
+ * and each chunk of out is copied back while later chunks compute.  Asynchronous with
+ * respect to the host: out is complete once `stream` has synchronized.  Copies overlap only
+ * with page-locked host memory; pageable memory gives the same results without overlap.
+ * Results equal tforge_gemm's on each chunk of rows (the kernel is chosen per chunk). */
+int tforge_gemm_host(const tforge_gemm_args *args, int64_t chunk_rows, void *stream);
+
 /* The three operator entries, in the reference's host-entry argument order. */
 int tforge_matmul(const float *A, const float *B, float *out, int64_t M, int64_t N, int64_t K,
                   int mode, void *stream);

@@ -53,6 +53,7 @@ class Config(C.Structure):
 _P, _I, _I64, _U64 = C.c_void_p, C.c_int, C.c_int64, C.c_uint64
 SIGNATURES = {
     "tforge_gemm": (_I, [C.POINTER(GemmArgs), _P]),
+    "tforge_gemm_host": (_I, [C.POINTER(GemmArgs), _I64, _P]),
     "tforge_matmul": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "tforge_mbr": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "tforge_matmul_add": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
@@ -135,6 +136,18 @@ def gemm(workload: str, A: int, B: int, out: int, M: int, N: int, K: int, mode: 
     args = GemmArgs(WORKLOADS[workload], MODES[mode], a_dtype, b_dtype, A, B, bias, c_res, out,
                     M, N, K, lda, ldb, ldc)
     check(lib().tforge_gemm(C.byref(args), stream), f"tforge_gemm({workload}, {M}x{N}x{K}, {mode})")
+
+
+def gemm_host(workload: str, A: int, B: int, out: int, M: int, N: int, K: int, mode: str = "fp32",
+              bias: int | None = None, c_res: int | None = None, stream: int | None = None,
+              chunk_rows: int = 0, a_dtype: int = F32, b_dtype: int = F32, lda: int = 0, ldb: int = 0,
+              ldc: int = 0) -> None:
+    """tforge_gemm_host on HOST pointers (ints): overlapped chunked copies and kernels,
+    asynchronous on `stream` (out is complete once the stream synchronizes)."""
+    args = GemmArgs(WORKLOADS[workload], MODES[mode], a_dtype, b_dtype, A, B, bias, c_res, out,
+                    M, N, K, lda, ldb, ldc)
+    check(lib().tforge_gemm_host(C.byref(args), chunk_rows, stream),
+          f"tforge_gemm_host({workload}, {M}x{N}x{K}, {mode})")
 
 
 def device_status(stream: int | None = None) -> int:

@@ -23,7 +23,7 @@ BUILD = PKG / "_build"
 LIB = PKG / "libtforge_gpu.so"
 RUNNER = PKG / "tforge-gpu-bench"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-LIB_SOURCES = ["tf_api.cu", "tf_gemm_tc.cu", "tf_gemm_2sm.cu", "tf_simt.cu", "tf_noalloc.cu"]
+LIB_SOURCES = ["tf_api.cu", "tf_gemm_tc.cu", "tf_gemm_2sm.cu", "tf_simt.cu", "tf_noalloc.cu", "tf_host.cu"]
 
 
 def nvcc() -> str:
@@ -44,7 +44,7 @@ def _newer(target: pathlib.Path, deps: list[pathlib.Path]) -> bool:
 
 def _compile(src: pathlib.Path) -> tuple[pathlib.Path, str]:
     obj = BUILD / (src.stem + ".o")
-    deps = [src, *CSRC.glob("*.cuh"), *CSRC.glob("*.h"), ROOT / "include" / "tforge.h"]
+    deps = [src, *CSRC.glob("*.cuh"), *CSRC.glob("*.h"), *CSRC.glob("*.inc"), ROOT / "include" / "tforge.h"]
     log = BUILD / (src.stem + ".ptxas.txt")
     if _newer(obj, deps) and log.exists():
         return obj, log.read_text()

@@ -3,11 +3,14 @@
 //
 // The dispatch table replaces the reference's analytical cost model and autotuner
 // (python/costmodel.py:49-97, bench/stage9_costmodel.py:63-154): the tile choice is a
-// function of (mode, M, N, K) over the instantiated tcgen05 configurations.
+// function of (mode, M, N, K) over the instantiated tcgen05 configurations -- the measured
+// winner of the offline sweep (tf_tune_table.inc) near a measured shape, an analytic wave
+// model elsewhere.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -153,7 +156,7 @@ struct Choice {
 
 // Stages per instantiated configuration: [prec][bn index] for one CTA; pair kernel.
 constexpr int kStages1[3][3] = {{4, 6, 8}, {2, 3, 4}, {4, 6, 8}};  // bn = 256, 128, 64
-constexpr int kStagesPair[3] = {6, 4, 6};                          // TF32, X3, BF16
+constexpr int kStagesPair[3] = {6, kPairX3Land, 6};                // TF32, X3, BF16
 
 // Relative throughput per busy SM of each kernel shape (pair, bn 256, 128, 64): wider
 // tiles read fewer operand bytes per FLOP, and the pair halves B per SM.
@@ -170,8 +173,48 @@ double est_cost(int64_t M, int64_t N, int tile_m, int tile_n, int ctas_per_tile,
   return (waves * per_wave_area > area ? waves * per_wave_area : area) / eff;
 }
 
-TcConfig table_tc(int prec, int64_t M, int64_t N, int64_t K) {
-  (void)K;
+bool config_supported(const TcConfig &c) {
+  if (c.pair) return c.bn == 256 && pair_smem_bytes(c.prec, c.stages) > 0;
+  return tc_config_supported(c);
+}
+
+// Measured choices of the offline sweep (python -m tensorforge_b200.autotune on a B200):
+// the fastest instantiated configuration that passed the FP64 check, per (prec, M, N, K).
+struct TuneEntry {
+  int prec;
+  int64_t m, n, k;
+  int pair, bn, stages;
+  double tflops;
+};
+const TuneEntry kTune[] = {
+#include "tf_tune_table.inc"
+    {-1, 1, 1, 1, 0, 0, 0, 0.0}};
+
+// The measured entry nearest to (M, N, K) in summed |log2| distance, provided each
+// dimension lies within a factor of two of it; false when none does.
+bool tuned_tc(int prec, int64_t M, int64_t N, int64_t K, TcConfig *out) {
+  const TuneEntry *hit = nullptr;
+  double best = 1e30;
+  for (const TuneEntry &e : kTune) {
+    if (e.prec != prec) continue;
+    const double dm = std::fabs(std::log2((double)M / (double)e.m));
+    const double dn = std::fabs(std::log2((double)N / (double)e.n));
+    const double dk = std::fabs(std::log2((double)K / (double)e.k));
+    if (dm > 1.0 || dn > 1.0 || dk > 1.0) continue;
+    if (dm + dn + dk < best) {
+      best = dm + dn + dk;
+      hit = &e;
+    }
+  }
+  if (!hit) return false;
+  const TcConfig c{prec, hit->bn, hit->stages, hit->pair};
+  if (!config_supported(c)) return false;
+  *out = c;
+  return true;
+}
+
+// Analytic fallback outside the measured range: the fewest waves over the tile area.
+TcConfig model_tc(int prec, int64_t M, int64_t N) {
   TcConfig best{prec, 256, kStagesPair[prec], 1};
   double best_cost = est_cost(M, N, 256, 256, 2, kKernelEff[0]);
   const int bns[3] = {256, 128, 64};
@@ -185,9 +228,10 @@ TcConfig table_tc(int prec, int64_t M, int64_t N, int64_t K) {
   return best;
 }
 
-bool config_supported(const TcConfig &c) {
-  if (c.pair) return c.bn == 256 && pair_smem_bytes(c.prec, c.stages) > 0;
-  return tc_config_supported(c);
+TcConfig table_tc(int prec, int64_t M, int64_t N, int64_t K) {
+  TcConfig c{};
+  if (tuned_tc(prec, M, N, K, &c)) return c;
+  return model_tc(prec, M, N);
 }
 
 Choice choose(int mode, int64_t M, int64_t N, int64_t K, bool tma_ok) {
@@ -317,6 +361,12 @@ int encode_operand_map(CUtensorMap *m, const void *base, bool bf16, int64_t rows
 }
 
 void set_last_error(const char *msg) { g_last_error = msg; }
+
+int check_gemm_args(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *ldc) {
+  return check_gemm(a, lda, ldb, ldc);
+}
+
+int device_pool(cudaMemPool_t *out) { return scratch_pool(out); }
 
 }  // namespace tf
 

@@ -7,24 +7,30 @@
 // A from both CTAs and B from both halves, so each SM reads only half of B per FLOP.
 //
 // fp32-accurate mode (3xTF32): per K step the MMA issues lo*hi, hi*lo and hi*hi.  The
-// split of A goes to tensor memory (tcgen05.st), so A crosses shared memory once and the
-// MMAs read only B from shared memory.  384 threads per CTA:
+// split of A goes to tensor memory (tcgen05.st), so the MMAs read only B from shared
+// memory.  Two rings: TMA lands raw A and B in a landing ring (kLand slots); converters
+// load a slot, free it at once, and write the split operands into an operand ring (kOps
+// slots: B hi and lo in shared memory, A hi and lo in TMEM), which the MMAs free.  So the
+// TMA round trip does not include the MMAs, and the MMA round trip does not include TMA.
+// 384 threads per CTA:
 //
-//   warp 0       TMA producer (each CTA): A tile and B half of each stage -> full[s].
-//   warps 2..11  converters (each CTA): the B half is split into hi (in place) and lo (a
-//                second buffer); warps 4..11 also split A: warp w takes rows
-//                32 (w % 4) .. +31 (its TMEM lane quadrant) and K half (w - 4) / 4, into
-//                TMEM columns [256 + 64 s, +32) (hi) and [+32, +32) (lo).  Then each warp
-//                arrives on this CTA's conv[s].
+//   warp 0       TMA producer (each CTA): A tile and B half of k-block kb -> landing slot
+//                kb % kLand (full[l]) once this CTA's converters freed it (lempty[l]).
+//   warps 2..11  converters (each CTA): load the landing slot, arrive lempty[l], wait
+//                until operand slot o = kb % kOps is free (empty[o]), write B hi and lo
+//                there; warps 4..11 also split A: warp w takes rows 32 (w % 4) .. +31 (its
+//                TMEM lane quadrant) and K half (w - 4) / 4, into TMEM columns
+//                [256 + 64 o, +32) (hi) and [+32, +32) (lo).  Then each warp arrives on
+//                this CTA's conv[o].
 //   warp 1       leader CTA: issues the pair MMAs into TMEM columns [0, 256) of both CTAs
-//                once its conv[s] and ready[s] (the peer's) completed; a multicast
-//                tcgen05.commit frees stage s in both CTAs (empty[s]), a last one signals
-//                accf in both.  Peer CTA: relays its conv[s] to the leader's ready[s] with
-//                one remote arrive per stage.
+//                once its conv[o] and ready[o] (the peer's) completed; a multicast
+//                tcgen05.commit frees operand slot o in both CTAs (empty[o]), a last one
+//                signals accf in both.  Peer CTA: relays its conv[o] to the leader's
+//                ready[o] with one st.async token per k-block.
 //   warps 4..11  epilogue (each CTA): its 128 rows x 256 columns from its own TMEM.
 //
 // The split (kPairSplit): the tensor core reads an f32 operand as TF32 by dropping its low
-// 13 mantissa bits, so the truncation split keeps hi = x (no store) and computes only
+// 13 mantissa bits, so the truncation split keeps hi = x and computes only
 // lo = x - trunc(x), exact in f32.  The round split (cvt.rna) is kept as an alternative.
 //
 // TF32 / BF16 modes have no converters: each CTA's TMA (.cta_group::2 form) completes on
@@ -49,11 +55,18 @@ constexpr int kPairSplit = TF_PAIR_SPLIT;
 
 namespace {
 
+#ifndef TF_PAIR_OPS
+#define TF_PAIR_OPS 3
+#endif
+// 3xTF32: depth of the operand ring (B hi/lo in shared memory, A hi/lo in TMEM).
+constexpr int kPairOps = TF_PAIR_OPS;
+
 template <int PREC, int STAGES>
 struct PairLayout {
   // 3xTF32: warps 0 producer, 1 MMA (leader) / relay (peer), 2..11 converters.
-  static constexpr int kThreads = PREC == PREC_X3 ? 384 : 256;
-  static constexpr int kEpiWarps = PREC == PREC_X3 ? 8 : 4;  // warps 4 .. 4 + kEpiWarps - 1
+  static constexpr bool kX3 = PREC == PREC_X3;
+  static constexpr int kThreads = kX3 ? 384 : 256;
+  static constexpr int kEpiWarps = kX3 ? 8 : 4;         // warps 4 .. 4 + kEpiWarps - 1
   static constexpr int kElem = PREC == PREC_BF16 ? 2 : 4;
   static constexpr int kBK = 128 / kElem;              // K elements per stage (one 128-B row)
   static constexpr int kUmmaK = 32 / kElem;            // K per MMA instruction
@@ -66,22 +79,32 @@ struct PairLayout {
   static constexpr int kABytes = 128 * 128;            // this CTA's 128 A rows
   static constexpr int kBBytes = kBNHalf * kBK * kElem;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kLoBytes = PREC == PREC_X3 ? kBBytes : 0;  // B lo (A lo lives in TMEM)
-  static constexpr int kRingBytes = STAGES * (kStageBytes + kLoBytes);
-  static constexpr int kNumBars = 4 * STAGES + 2;      // full, conv, ready, empty, accf, resf
+  // Landing ring (TMA destination): kLand slots of A + B.  TF32/BF16: the MMA reads them
+  // in place.  3xTF32: the converters empty a slot as soon as they have loaded it, into the
+  // operand ring of kOps slots -- B hi and B lo in shared memory, A hi and lo in TMEM --
+  // which the MMAs empty.  TMA latency then overlaps the MMAs of the operand ring.
+  static constexpr int kLand = STAGES;
+  static constexpr int kOps = kX3 ? kPairOps : STAGES;
+  static constexpr int kOpBytes = kX3 ? 2 * kBBytes : 0;
+  static constexpr int kRingBytes = kLand * kStageBytes + kOps * kOpBytes;
+  // Barriers: full[kLand], lempty[kLand] (3xTF32: converters -> producer), conv[kOps],
+  // ready[kOps], empty[kOps] (MMA commit), accf, resf.
+  static constexpr int kNumBars = 2 * kLand + 3 * kOps + 2;
   // barriers, then tmem slot, abort flag, epilogue flag, spare, and one mailbox word per
-  // stage (the peer's st.async tokens land there).
-  static constexpr int kBarBytes = 8 * kNumBars + 16 + 4 * STAGES;
+  // operand stage (the peer's st.async tokens land there).
+  static constexpr int kBarBytes = 8 * kNumBars + 16 + 4 * kOps;
   static constexpr int kSmemBytes = 1024 + kRingBytes + kBarBytes;
   static constexpr uint32_t kAccCols = 256;
-  static constexpr uint32_t kTmemCols = PREC == PREC_X3 ? 512u : 256u;
+  static constexpr uint32_t kTmemCols = kX3 ? 512u : 256u;
   static constexpr int kConvWarps = 10;                // warps 2..11 (3xTF32)
-  __host__ __device__ static constexpr int a_off(int s) { return s * kStageBytes; }
-  __host__ __device__ static constexpr int b_off(int s) { return s * kStageBytes + kABytes; }
-  __host__ __device__ static constexpr int lo_off(int s) { return STAGES * kStageBytes + s * kLoBytes; }
+  __host__ __device__ static constexpr int a_off(int l) { return l * kStageBytes; }
+  __host__ __device__ static constexpr int b_off(int l) { return l * kStageBytes + kABytes; }
+  __host__ __device__ static constexpr int hi_off(int o) { return kLand * kStageBytes + o * kOpBytes; }
+  __host__ __device__ static constexpr int lo_off(int o) { return hi_off(o) + kBBytes; }
   __host__ __device__ static constexpr int bar_off() { return kRingBytes; }
-  __host__ __device__ static constexpr uint32_t a_tmem_col(int s) { return kAccCols + 64u * s; }
-  static_assert(PREC != PREC_X3 || kAccCols + 64u * STAGES <= 512u, "TMEM budget");
+  __host__ __device__ static constexpr uint32_t a_tmem_col(int o) { return kAccCols + 64u * o; }
+  static_assert(!kX3 || kAccCols + 64u * kOps <= 512u, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
   // Epilogue staging: eight 128-row x 32-column f32 boxes (16 KB each) reuse the ring.
   static constexpr int kEpiBoxBytes = 128 * 128;
   static_assert(8 * kEpiBoxBytes <= kRingBytes, "epilogue staging fits in the ring");
@@ -91,6 +114,32 @@ struct PairLayout {
 __device__ __forceinline__ void pause_ns(uint64_t ns) {
   const uint64_t t0 = globaltimer();
   while (globaltimer() - t0 < ns) __nanosleep(1000);
+}
+
+// 3xTF32 split of four f32 values into hi + lo.  SPLIT 1 (truncation): the tensor core
+// reads an f32 operand as TF32 by dropping the low 13 mantissa bits, so hi = x as stored
+// and lo = x - trunc(x) (exact); non-finite inputs take the per-element path.  SPLIT 0
+// (round): hi = rna(x), lo = rna(x - hi).
+template <int SPLIT>
+__device__ __forceinline__ void split4(const float4 x, float4 &hi, float4 &lo) {
+  if constexpr (SPLIT == 1) {
+    bool special;
+    lo = split_lo_trunc4(x, special);
+    hi = x;
+    if (special) {
+      lo = make_float4(split_lo_trunc(x.x), split_lo_trunc(x.y), split_lo_trunc(x.z), split_lo_trunc(x.w));
+      hi = make_float4(__uint_as_float(split_hi_trunc_bits(__float_as_uint(x.x))),
+                       __uint_as_float(split_hi_trunc_bits(__float_as_uint(x.y))),
+                       __uint_as_float(split_hi_trunc_bits(__float_as_uint(x.z))),
+                       __uint_as_float(split_hi_trunc_bits(__float_as_uint(x.w))));
+    }
+  } else {
+    hi = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+    lo.x = isfinite(hi.x) ? to_tf32(x.x - hi.x) : 0.f;
+    lo.y = isfinite(hi.y) ? to_tf32(x.y - hi.y) : 0.f;
+    lo.z = isfinite(hi.z) ? to_tf32(x.z - hi.z) : 0.f;
+    lo.w = isfinite(hi.w) ? to_tf32(x.w - hi.w) : 0.f;
+  }
 }
 
 // Peer CTA of a 3xTF32 pair: forwards "this CTA's converters finished stage kb" (local
@@ -122,11 +171,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
                                               ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::bar_off());
-  // full[s]: TMA bytes landed (3xTF32: this CTA's; otherwise the leader's barrier counts
-  // both CTAs' bytes); conv[s]: this CTA's converters done; ready[s] (leader): the peer's
-  // converters done; empty[s]: the pair MMAs reading stage s done; accf: accumulator done.
-  const uint32_t full0 = smem_u32(bars), conv0 = full0 + 8 * STAGES, ready0 = conv0 + 8 * STAGES,
-                 empty0 = ready0 + 8 * STAGES, accf = empty0 + 8 * STAGES, resf = accf + 8;
+  // full[l]: TMA bytes of landing slot l arrived (3xTF32: this CTA's; otherwise the
+  // leader's barrier counts both CTAs' bytes); lempty[l] (3xTF32): this CTA's converters
+  // have loaded slot l; conv[o]: this CTA's converters filled operand slot o; ready[o]
+  // (leader): the peer's converters did; empty[o]: the pair MMAs reading operand slot o
+  // are done (TF32/BF16: operand slot = landing slot); accf: accumulator done.
+  constexpr int kL = L::kLand, kO = L::kOps;
+  const uint32_t full0 = smem_u32(bars), lempty0 = full0 + 8 * kL, conv0 = lempty0 + 8 * kL,
+                 ready0 = conv0 + 8 * kO, empty0 = ready0 + 8 * kO, accf = empty0 + 8 * kO, resf = accf + 8;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile uint32_t *abort_flag = tmem_slot + 1;
   const uint32_t mailbox0 = smem_u32(tmem_slot + 4);
@@ -138,11 +190,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   const WaitCtl wc{abort_flag, p.status, p.limit_ns};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(conv0 + 8 * s, L::kConvWarps);
-      mbar_init(ready0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 1);
+    for (int l = 0; l < kL; ++l) {
+      mbar_init(full0 + 8 * l, 1);
+      mbar_init(lempty0 + 8 * l, L::kConvWarps);
+    }
+    for (int o = 0; o < kO; ++o) {
+      mbar_init(conv0 + 8 * o, L::kConvWarps);
+      mbar_init(ready0 + 8 * o, 1);
+      mbar_init(empty0 + 8 * o, 1);
     }
     mbar_init(accf, 1);
     mbar_init(resf, 1);
@@ -165,13 +220,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
-    // 3xTF32: loads complete on this CTA's full[s] (its converters consume them).
-    // TF32/BF16: loads complete on the LEADER's full[s], which expects both CTAs' bytes.
+    // 3xTF32: loads complete on this CTA's full[l]; the slot is reused once this CTA's
+    // converters have loaded it (lempty[l]).  TF32/BF16: loads complete on the LEADER's
+    // full[l], which expects both CTAs' bytes; the slot is reused once the pair MMAs that
+    // read it are done (empty[l], committed to both CTAs).
     const uint32_t lead_full0 = map_to_cta(full0, 0);
     int kb = 0;
     for (; kb < nkb; ++kb) {
-      const int s = kb % STAGES, round = kb / STAGES;
-      if (round > 0 && !mbar_wait_cluster(empty0 + 8 * s, (round - 1) & 1, wc)) break;
+      const int s = kb % kL, round = kb / kL;
+      if (round > 0) {
+        const bool ok = kX3 ? mbar_wait(lempty0 + 8 * s, (round - 1) & 1, wc)
+                            : mbar_wait_cluster(empty0 + 8 * s, (round - 1) & 1, wc);
+        if (!ok) break;
+      }
       if (p.debug_skip && kb == 0) continue;  // test hook: this stage never fills
       const int kc = kb * L::kBK;
       const int nb = n0 + (int)rank * L::kBNHalf;
@@ -193,11 +254,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
     if (*abort_flag) {
       if (kX3 || rank == 0) {
 #pragma unroll 1
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < kL; ++s) {
           if (kb - 1 < s) continue;
-          const int last = kb - 1 - ((kb - 1 - s) % STAGES);
+          const int last = kb - 1 - ((kb - 1 - s) % kL);
           if (p.debug_skip && last == 0) continue;
-          mbar_wait_drain_cluster(full0 + 8 * s, (last / STAGES) & 1, p.limit_ns);
+          mbar_wait_drain_cluster(full0 + 8 * s, (last / kL) & 1, p.limit_ns);
         }
       } else {
         pause_ns(200000);  // the peer's loads complete on the leader's barrier
@@ -208,7 +269,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       // ---------------- pair MMA issuer (leader CTA) ----------------
       uint32_t accum = 0;
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
+        const int s = kb % kO, round = kb / kO;
         if constexpr (kX3) {
           if (!mbar_wait(conv0 + 8 * s, round & 1, wc)) break;
           mbar_arrive_expect_tx(ready0 + 8 * s, 4);  // the peer's token for this round
@@ -219,17 +280,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < L::kKSteps; ++ks) {
-          const uint64_t bd = smem_desc(sbase + L::b_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
-                                        L::kBSbo, L::kBSwz);
           if constexpr (kX3) {
             const uint32_t a_hi = tmem + L::a_tmem_col(s) + 8 * ks, a_lo = a_hi + 32;
             const uint64_t bl = smem_desc(sbase + L::lo_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
                                           L::kBSbo, L::kBSwz);
-            mma_ts_pair_tf32(tmem, a_lo, bd, kIdesc, accum);
+            const uint64_t bh = smem_desc(sbase + L::hi_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
+                                          L::kBSbo, L::kBSwz);
+            mma_ts_pair_tf32(tmem, a_lo, bh, kIdesc, accum);
             mma_ts_pair_tf32(tmem, a_hi, bl, kIdesc, 1u);
-            mma_ts_pair_tf32(tmem, a_hi, bd, kIdesc, 1u);
+            mma_ts_pair_tf32(tmem, a_hi, bh, kIdesc, 1u);
           } else {
             const uint64_t ad = smem_desc(sbase + L::a_off(s) + ks * 32, 16, 1024, 2);
+            const uint64_t bd = smem_desc(sbase + L::b_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
+                                          L::kBSbo, L::kBSwz);
             mma_ss_pair<kTF32>(tmem, ad, bd, kIdesc, accum);
           }
           accum = 1u;
@@ -239,112 +302,73 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       mma_commit_pair(accf, 0x3);
       if (*abort_flag) mbar_wait_drain_cluster(accf, 0, p.limit_ns);
     } else if constexpr (kX3) {
-      relay_stages<STAGES>(conv0, ready0, mailbox0, nkb, wc);
+      relay_stages<kO>(conv0, ready0, mailbox0, nkb, wc);
     }
   } else if (kX3 && warp >= 2) {
     // ---------------- 3xTF32 converters (both CTAs, warps 2..11) ----------------
+    // k-block kb: landing slot l = kb % kLand, operand slot o = kb % kOps.  Each thread
+    // loads its B chunks (t + 320 i) and, in warps 4..11, four 16-B chunks of A row r (K
+    // half h), and releases the landing slot (lempty[l]) before it splits.  It then waits
+    // until the MMAs of k-block kb - kOps have finished with operand slot o (empty[o]) and
+    // writes B hi and lo there at the offsets TMA used (same swizzle), and A hi and lo into
+    // the TMEM columns of slot o.
     const int t = threadIdx.x - 64;
     constexpr int kChunks = L::kBBytes / 16;
-    const int q = warp & 3, h = (warp - 4) >> 2, r = q * 32 + lane;  // A: row r, K half h
+    const int q = warp & 3, h = (warp - 4) >> 2, r = q * 32 + lane;
     for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % STAGES, round = kb / STAGES;
-      if (!mbar_wait(full0 + 8 * s, round & 1, wc)) break;
-      float4 *braw = reinterpret_cast<float4 *>(smem + L::b_off(s));
-      float4 *blo = reinterpret_cast<float4 *>(smem + L::lo_off(s));
-      // Row r of the A tile: 128 B at r * 128, 16-B chunk j stored at j ^ (r % 8); warps
-      // 4..11 split K elements [16 h, 16 h + 16) of their row into TMEM columns of stage s.
-      const uint8_t *arow = smem + L::a_off(s) + r * 128;
-      if constexpr (SPLIT == 1) {
-        // All shared-memory loads of this thread first (B: chunks t + 320 i; A: 4 chunks),
-        // then the 2-op truncation split, so the warp keeps several loads in flight.
-        float4 xb[4], xa[4];
+      const int l = kb % kL, o = kb % kO;
+      if (!mbar_wait(full0 + 8 * l, (kb / kL) & 1, wc)) break;
+      const float4 *braw = reinterpret_cast<const float4 *>(smem + L::b_off(l));
+      // Row r of the A tile: 128 B at r * 128, 16-B chunk j stored at j ^ (r % 8).
+      const uint8_t *arow = smem + L::a_off(l) + r * 128;
+      float4 xb[4], xa[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (t + 320 * i < kChunks) xb[i] = braw[t + 320 * i];
-        if (warp >= 4) {
+      for (int i = 0; i < 4; ++i)
+        if (t + 320 * i < kChunks) xb[i] = braw[t + 320 * i];
+      if (warp >= 4) {
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj)
-            xa[jj] = *reinterpret_cast<const float4 *>(arow + (((4 * h + jj) ^ (r & 7)) << 4));
+        for (int jj = 0; jj < 4; ++jj)
+          xa[jj] = *reinterpret_cast<const float4 *>(arow + (((4 * h + jj) ^ (r & 7)) << 4));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(lempty0 + 8 * l);
+      if (kb >= kO && !mbar_wait_cluster(empty0 + 8 * o, ((kb / kO) - 1) & 1, wc)) break;
+      float4 *bhi = reinterpret_cast<float4 *>(smem + L::hi_off(o));
+      float4 *blo = reinterpret_cast<float4 *>(smem + L::lo_off(o));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = t + 320 * i;
+        if (c < kChunks) {
+          float4 hh, ll;
+          split4<SPLIT>(xb[i], hh, ll);
+          bhi[c] = hh;
+          blo[c] = ll;
         }
+      }
+      fence_proxy_async_smem();
+      if (warp >= 4) {
+        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = t + 320 * i;
-          if (c < kChunks) {
-            bool special;
-            blo[c] = split_lo_trunc4(xb[i], special);
-            if (special) {  // a non-finite element (rare): exact per-element handling
-              blo[c] = make_float4(split_lo_trunc(xb[i].x), split_lo_trunc(xb[i].y),
-                                   split_lo_trunc(xb[i].z), split_lo_trunc(xb[i].w));
-              braw[c] = make_float4(__uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].x))),
-                                    __uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].y))),
-                                    __uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].z))),
-                                    __uint_as_float(split_hi_trunc_bits(__float_as_uint(xb[i].w))));
-            }
-          }
+        for (int jj = 0; jj < 4; ++jj) {
+          float4 hh, ll;
+          split4<SPLIT>(xa[jj], hh, ll);
+          hi[4 * jj + 0] = __float_as_uint(hh.x);
+          hi[4 * jj + 1] = __float_as_uint(hh.y);
+          hi[4 * jj + 2] = __float_as_uint(hh.z);
+          hi[4 * jj + 3] = __float_as_uint(hh.w);
+          lo[4 * jj + 0] = __float_as_uint(ll.x);
+          lo[4 * jj + 1] = __float_as_uint(ll.y);
+          lo[4 * jj + 2] = __float_as_uint(ll.z);
+          lo[4 * jj + 3] = __float_as_uint(ll.w);
         }
-        fence_proxy_async_smem();
-        if (warp >= 4) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            bool special;
-            const float4 l = split_lo_trunc4(xa[jj], special);
-            const float xs[4] = {xa[jj].x, xa[jj].y, xa[jj].z, xa[jj].w};
-            const float ls[4] = {l.x, l.y, l.z, l.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              hi[4 * jj + i] = __float_as_uint(xs[i]);
-              lo[4 * jj + i] = __float_as_uint(ls[i]);
-            }
-            if (special) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                hi[4 * jj + i] = split_hi_trunc_bits(__float_as_uint(xs[i]));
-                lo[4 * jj + i] = __float_as_uint(split_lo_trunc(xs[i]));
-              }
-            }
-          }
-          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + L::a_tmem_col(s) + 16 * h;
-          tmem_st_32x32b_x16(ta, hi);
-          tmem_st_32x32b_x16(ta + 32, lo);
-          tmem_st_wait();
-        }
-      } else {
-#pragma unroll 2
-        for (int c = t; c < kChunks; c += 320) {
-          const float4 x = braw[c];
-          float4 hh, l;
-          hh.x = to_tf32(x.x); hh.y = to_tf32(x.y); hh.z = to_tf32(x.z); hh.w = to_tf32(x.w);
-          l.x = isfinite(hh.x) ? to_tf32(x.x - hh.x) : 0.f;
-          l.y = isfinite(hh.y) ? to_tf32(x.y - hh.y) : 0.f;
-          l.z = isfinite(hh.z) ? to_tf32(x.z - hh.z) : 0.f;
-          l.w = isfinite(hh.w) ? to_tf32(x.w - hh.w) : 0.f;
-          braw[c] = hh;
-          blo[c] = l;
-        }
-        fence_proxy_async_smem();
-        if (warp >= 4) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const float4 v = *reinterpret_cast<const float4 *>(arow + (((4 * h + jj) ^ (r & 7)) << 4));
-            const float xs[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float hv = to_tf32(xs[i]);
-              hi[4 * jj + i] = __float_as_uint(hv);
-              lo[4 * jj + i] = __float_as_uint(isfinite(hv) ? to_tf32(xs[i] - hv) : 0.f);
-            }
-          }
-          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + L::a_tmem_col(s) + 16 * h;
-          tmem_st_32x32b_x16(ta, hi);
-          tmem_st_32x32b_x16(ta + 32, lo);
-          tmem_st_wait();
-        }
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + L::a_tmem_col(o) + 16 * h;
+        tmem_st_32x32b_x16(ta, hi);
+        tmem_st_32x32b_x16(ta + 32, lo);
+        tmem_st_wait();
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(conv0 + 8 * s);
+      if (lane == 0) mbar_arrive(conv0 + 8 * o);
     }
   }
 
@@ -478,7 +502,7 @@ cudaError_t pair_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
 }  // namespace
 
 // Instantiated pair configurations: (precision, stages).
-#define TF_PAIR_CONFIGS(X) X(PREC_X3, 4) X(PREC_TF32, 6) X(PREC_BF16, 6)
+#define TF_PAIR_CONFIGS(X) X(PREC_X3, kPairX3Land) X(PREC_TF32, 6) X(PREC_BF16, 6)
 
 int pair_smem_bytes(int prec, int stages) {
 #define TF_PSMEM(P, S) \

@@ -5,11 +5,19 @@
 
 #include <cstdint>
 
+#include "tforge.h"
+
 namespace tf {
 
 enum Epi : int { EPI_MATMUL = 0, EPI_MBR = 1, EPI_ADD = 2 };
 // Tensor-core precision paths: one TF32 product, the 3xTF32 split, or bf16 operands.
 enum Prec : int { PREC_TF32 = 0, PREC_X3 = 1, PREC_BF16 = 2 };
+
+#ifndef TF_PAIR_X3_LAND
+#define TF_PAIR_X3_LAND 4
+#endif
+// Landing-ring depth of the 3xTF32 pair kernel (its instantiated "stages").
+constexpr int kPairX3Land = TF_PAIR_X3_LAND;
 
 // Parameters of the tcgen05 kernel besides the two tensor maps.
 struct TcParams {
@@ -61,6 +69,10 @@ bool select_tc_config(int mode, int64_t M, int64_t N, int64_t K, TcConfig *out);
 int encode_operand_map(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols,
                        int64_t ld, uint32_t box_cols, uint32_t box_rows, bool atom32);
 void set_last_error(const char *msg);
+// tforge_gemm's argument checks (pointers are only compared, never dereferenced) and the
+// library's per-device stream-ordered memory pool.
+int check_gemm_args(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *ldc);
+int device_pool(cudaMemPool_t *out);
 
 // SIMT sequential-k FFMA GEMM (bitwise equal to the reference's generated kernels).
 cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const float *aux, float *C,

@@ -73,12 +73,27 @@ def test_pitch_smaller_than_row_is_rejected():
     assert _lib.lib().tforge_gemm(C.byref(args), None) == _lib.ERR_SHAPE
 
 
+def test_host_entry_validates_before_any_cuda_call():
+    """tforge_gemm_host applies tforge_gemm's checks to its host pointers first."""
+    L = _lib.lib()
+    assert L.tforge_gemm_host(None, 0, None) == _lib.ERR_NULL
+    args = _lib.GemmArgs(0, 0, _lib.F32, _lib.F32, P, 2 * P, None, None, 4 * P, 8, 8, 8, 4, 0, 0)
+    assert L.tforge_gemm_host(C.byref(args), 0, None) == _lib.ERR_SHAPE
+    args = _lib.GemmArgs(1, 0, _lib.F32, _lib.F32, P, 2 * P, None, None, 4 * P, 8, 8, 8, 0, 0, 0)
+    assert L.tforge_gemm_host(C.byref(args), 0, None) == _lib.ERR_NULL  # mbr without bias
+    args = _lib.GemmArgs(0, 0, _lib.F32, _lib.F32, P, 2 * P, None, None, P, 8, 8, 8, 0, 0, 0)
+    assert L.tforge_gemm_host(C.byref(args), 0, None) == _lib.ERR_ALIAS  # out overlaps A
+    args = _lib.GemmArgs(0, 0, _lib.F32, _lib.F32, None, None, None, None, None, 0, 8, 8, 0, 0, 0)
+    assert L.tforge_gemm_host(C.byref(args), 0, None) == _lib.OK
+
+
 @pytest.mark.parametrize("shape,mode,kernel", [
     ((2048, 2048, 2048), "fp32", "tf_gemm_tcgen05_3xtf32_pair"),
     ((2048, 2048, 2048), "tf32", "tf_gemm_tcgen05_tf32_pair"),
     ((2048, 2048, 2048), "bf16", "tf_gemm_tcgen05_bf16_pair"),
-    ((256, 256, 128), "fp32", "tf_gemm_tcgen05_3xtf32"),
-    ((300, 8, 64), "tf32", "tf_gemm_tcgen05_tf32"),
+    ((256, 256, 128), "fp32", "tf_gemm_tcgen05_3xtf32_pair"),  # measured: pair beats 1-CTA
+    ((1000, 1000, 1000), "bf16", "tf_gemm_tcgen05_bf16"),       # measured: 128x64 tiles
+    ((300, 8, 64), "tf32", "tf_gemm_tcgen05_tf32"),             # outside the table: the model
     ((2048, 2048, 2048), "fp32_exact", "tf_gemm_simt_ffma"),
     ((777, 1111, 333), "fp32", "tf_gemm_simt_ffma"),   # pitches not 16-byte multiples
     ((256, 256, 8), "fp32", "tf_gemm_simt_ffma"),      # K < 16: exact kernel keeps the fp32 bound
@@ -97,6 +112,29 @@ def test_dispatch_table(shape, mode, kernel):
         assert d["tmem_cols"] <= 512
         if not pair:
             assert d["tmem_cols"] == d["tile"][1]
+
+
+def _tune_table():
+    text = (pathlib.Path(tg.PKG) / "csrc" / "tf_tune_table.inc").read_text()
+    rows = re.findall(r"\{(\d+), (\d+), (\d+), (\d+), (\d+), (\d+), (\d+), ([0-9.]+)\}", text)
+    return [tuple(int(x) for x in r[:7]) + (float(r[7]),) for r in rows]
+
+
+def test_tuned_table_entries_are_what_dispatch_picks():
+    """Every measured entry is a supported configuration and the dispatch returns it for
+    its own shape; shapes within a factor of two take the nearest entry."""
+    entries = _tune_table()
+    assert len(entries) >= 60
+    modes = {0: "tf32", 1: "fp32", 2: "bf16"}
+    for prec, m, n, k, pair, bn, stages, tflops in entries:
+        assert tflops > 0
+        d = _lib.describe("mbr", m, n, k, modes[prec])
+        assert d["kernel"].endswith("_pair") == bool(pair), (prec, m, n, k)
+        assert d["stages"] == stages
+        if not pair:
+            assert d["tile"][1] == bn
+    # (1100, 1000, 904) is nearest to the measured (1000, 1000, 1000) bf16 entry.
+    assert _lib.describe("mbr", 1100, 1000, 904, "bf16")["tile"][1] == 64
 
 
 def test_forced_config_and_reset():
