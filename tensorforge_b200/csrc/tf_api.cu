@@ -207,7 +207,8 @@ bool tuned_tc(int prec, int64_t M, int64_t N, int64_t K, TcConfig *out) {
     }
   }
   if (!hit) return false;
-  const TcConfig c{prec, hit->bn, hit->stages, hit->pair};
+  // The pair kernel has one instantiated depth per precision; the table says pair or not.
+  const TcConfig c{prec, hit->bn, hit->pair ? kStagesPair[prec] : hit->stages, hit->pair};
   if (!config_supported(c)) return false;
   *out = c;
   return true;
@@ -554,7 +555,7 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
   out->grid[0] = (int)((N + c.tc.bn - 1) / c.tc.bn) * (c.tc.pair ? 2 : 1);
   out->grid[1] = (int)((M + tm - 1) / tm);
   out->grid[2] = 1;
-  out->block[0] = 256;
+  out->block[0] = c.tc.pair && c.tc.prec == PREC_X3 ? 384 : 256;  // 3xTF32 pair: 12 warps
   out->block[1] = out->block[2] = 1;
   out->cluster[0] = c.tc.pair ? 2 : 1;
   out->smem_bytes = c.tc.pair ? pair_smem_bytes(c.tc.prec, c.tc.stages) : tc_smem_bytes(c.tc);

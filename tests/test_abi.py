@@ -102,7 +102,7 @@ def test_host_entry_validates_before_any_cuda_call():
 def test_dispatch_table(shape, mode, kernel):
     d = _lib.describe("mbr", *shape, mode)
     assert d["kernel"] == kernel
-    assert d["block"] == [256, 1, 1]
+    assert d["block"] == [384 if kernel == "tf_gemm_tcgen05_3xtf32_pair" else 256, 1, 1]
     if kernel.startswith("tf_gemm_tcgen05"):
         m, n, _ = shape
         pair = kernel.endswith("_pair")
@@ -130,9 +130,8 @@ def test_tuned_table_entries_are_what_dispatch_picks():
         assert tflops > 0
         d = _lib.describe("mbr", m, n, k, modes[prec])
         assert d["kernel"].endswith("_pair") == bool(pair), (prec, m, n, k)
-        assert d["stages"] == stages
-        if not pair:
-            assert d["tile"][1] == bn
+        if not pair:  # the pair kernel has one instantiated depth per precision
+            assert d["stages"] == stages and d["tile"][1] == bn
     # (1100, 1000, 904) is nearest to the measured (1000, 1000, 1000) bf16 entry.
     assert _lib.describe("mbr", 1100, 1000, 904, "bf16")["tile"][1] == 64
 
