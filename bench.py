@@ -435,9 +435,34 @@ def cublas_comparator(m, n, k, A, B, bias, flush, stream):
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1))
         med = statistics.median(ts)
-        return {"cublas_sgemm_plus_bias_relu": {"tflops": 2.0 * m * n * k / (med * 1e-3) / 1e12, "ms": med}}
+        out = {"cublas_sgemm_plus_bias_relu": {"tflops": 2.0 * m * n * k / (med * 1e-3) / 1e12, "ms": med}}
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+    out.update(runner_comparators(m, n, k))
+    return out
+
+
+def runner_comparators(m, n, k):
+    """More cuBLAS paths through the runner (same GPU, L2 flushed, median of 20): FP32
+    emulated on bf16 tensor cores (CUBLAS_COMPUTE_32F_EMULATED_16BFX9), the fp32-accurate
+    comparator closest to this mode, and cuBLASLt TF32 with the bias + relu fused into its
+    epilogue (TF32 precision, for context)."""
+    import subprocess
+
+    runner = pathlib.Path(__file__).resolve().parent / "tensorforge_b200" / "tforge-gpu-bench"
+    res = {}
+    for key, math in (("cublas_fp32_emulated_bf16x9_plus_bias_relu", "bf16x9"),
+                      ("cublaslt_tf32_relu_bias_epilogue", "lt_tf32")):
+        cmd = [str(runner), "--mode", "cublas", "--math", math, "--workload", "mbr", "--m", str(m), "--n", str(n),
+               "--k", str(k), "--warmup", "5", "--reps", "20", "--flush"]
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+            d = json.loads(r.stdout) if r.returncode == 0 else None
+        except (OSError, ValueError, subprocess.TimeoutExpired):
+            d = None
+        if d:
+            res[key] = {"tflops": d["tflops"], "ms": d["median_ms"], "kernel": d["kernel"]}
+    return res
 
 
 def e2e_measure(L, _lib, m, n, k, mode, A, B, bias, world, dev, steps=20, warmup=3):

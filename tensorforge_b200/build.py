@@ -75,7 +75,7 @@ def build(force: bool = False) -> pathlib.Path:
     runner_src = CSRC / "runner" / "tforge_gpu_bench.cu"
     if runner_src.exists() and not _newer(RUNNER, [runner_src, LIB, ROOT / "include" / "tforge.h"]):
         cmd = [nvcc(), *_flags(), str(runner_src), "-o", str(RUNNER), "-L", str(PKG), "-ltforge_gpu",
-               f"-Xlinker=-rpath,$ORIGIN", "-lcublas", "-lcuda", "-ldl"]
+               f"-Xlinker=-rpath,$ORIGIN", "-lcublasLt", "-lcublas", "-lcuda", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("runner build failed:\n" + r.stderr)

@@ -7,7 +7,12 @@
 //
 //   tforge-gpu-bench --mode lib --workload mbr --m M --n N --k K [--precision fp32|tf32|bf16|fp32_exact]
 //       [--kernel pair|cta|simt --bn 256 --stages 4] [--warmup 10 --reps 100 --flush] [--in-dir d --out o.bin] [--seed S]
-//   tforge-gpu-bench --mode cublas --workload mbr --m M --n N --k K [--math default|tf32|bf16]
+//   tforge-gpu-bench --mode cublas --workload mbr --m M --n N --k K
+//       [--math default|tf32|bf16|bf16x9|lt|lt_tf32]
+//     default: cublasSgemm (FP32 FMA) + separate bias/relu -- the reference's comparator;
+//     tf32 / bf16: TF32 tensor-op math / bf16 inputs with f32 accumulation;
+//     bf16x9: FP32 emulated on bf16 tensor cores (CUBLAS_COMPUTE_32F_EMULATED_16BFX9, eager);
+//     lt / lt_tf32: cuBLASLt FP32 / TF32 with the bias + relu fused into its epilogue.
 //   tforge-gpu-bench ... --info-only        (launch description and occupancy, no run)
 //
 // Buffers follow the host entry's argument order (runners/gpu/tforge-gpu-bench.cu:20-24):
@@ -16,6 +21,7 @@
 // mt19937(seed) U[-1,1] in the reference's order.  Timing: CUDA events around each rep
 // on one stream, warm-up reps untimed, optional 256 MiB L2 flush outside the timed
 // region, NVML SM clock and power sampled after every rep (loaded at run time).
+#include <cublasLt.h>
 #include <cublas_v2.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -251,6 +257,11 @@ int main(int argc, char **argv) {
   std::function<void()> run;
   cublasHandle_t blas = nullptr;
   __nv_bfloat16 *abf = nullptr, *bbf = nullptr;
+  cublasLtHandle_t lt = nullptr;
+  cublasLtMatmulDesc_t ltDesc = nullptr;
+  cublasLtMatrixLayout_t ltA = nullptr, ltB = nullptr, ltC = nullptr;
+  cublasLtMatmulHeuristicResult_t ltHeur{};
+  void *ltWs = nullptr;
   std::string kernel = L.kernel;
 
   if (a.mode == "lib") {
@@ -281,11 +292,58 @@ int main(int argc, char **argv) {
       cuda_ok(cudaMalloc(&abf, M * K * 2), "cudaMalloc");
       cuda_ok(cudaMalloc(&bbf, K * N * 2), "cudaMalloc");
       kernel = "cublasGemmEx(bf16 in, f32 acc)";
+    } else if (a.math == "bf16x9") {
+      blas_ok(cublasSetEmulationStrategy(blas, CUBLAS_EMULATION_STRATEGY_EAGER), "cublasSetEmulationStrategy");
+      kernel = "cublasGemmEx(f32, COMPUTE_32F_EMULATED_16BFX9)";
+    } else if (a.math == "lt" || a.math == "lt_tf32") {
+      if (wl == TFORGE_MATMUL_ADD) die("--math lt* covers matmul and mbr");
+      blas_ok(cublasLtCreate(&lt), "cublasLtCreate");
+      const cublasComputeType_t ct = a.math == "lt" ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_FAST_TF32;
+      blas_ok(cublasLtMatmulDescCreate(&ltDesc, ct, CUDA_R_32F), "cublasLtMatmulDescCreate");
+      const cublasOperation_t opN = CUBLAS_OP_N;
+      blas_ok(cublasLtMatmulDescSetAttribute(ltDesc, CUBLASLT_MATMUL_DESC_TRANSA, &opN, sizeof(opN)), "TRANSA");
+      blas_ok(cublasLtMatmulDescSetAttribute(ltDesc, CUBLASLT_MATMUL_DESC_TRANSB, &opN, sizeof(opN)), "TRANSB");
+      if (wl == TFORGE_MBR) {
+        // Column-major view C^T (N x M): the bias runs along its rows, i.e. our columns.
+        const cublasLtEpilogue_t epi = CUBLASLT_EPILOGUE_RELU_BIAS;
+        blas_ok(cublasLtMatmulDescSetAttribute(ltDesc, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof(epi)), "EPILOGUE");
+        blas_ok(cublasLtMatmulDescSetAttribute(ltDesc, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &dBias, sizeof(dBias)),
+                "BIAS_POINTER");
+      }
+      blas_ok(cublasLtMatrixLayoutCreate(&ltB, CUDA_R_32F, N, K, N), "layout B");
+      blas_ok(cublasLtMatrixLayoutCreate(&ltA, CUDA_R_32F, K, M, K), "layout A");
+      blas_ok(cublasLtMatrixLayoutCreate(&ltC, CUDA_R_32F, N, M, N), "layout C");
+      cublasLtMatmulPreference_t pref;
+      blas_ok(cublasLtMatmulPreferenceCreate(&pref), "pref");
+      const size_t wsBytes = size_t(64) << 20;
+      blas_ok(cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &wsBytes,
+                                                   sizeof(wsBytes)),
+              "pref workspace");
+      cuda_ok(cudaMalloc(&ltWs, wsBytes), "cudaMalloc(lt workspace)");
+      int found = 0;
+      blas_ok(cublasLtMatmulAlgoGetHeuristic(lt, ltDesc, ltB, ltA, ltC, ltC, pref, 1, &ltHeur, &found), "heuristic");
+      if (!found) die("cuBLASLt: no algorithm");
+      cublasLtMatmulPreferenceDestroy(pref);
+      kernel = a.math == "lt" ? "cublasLtMatmul(f32, RELU_BIAS epilogue)" : "cublasLtMatmul(tf32, RELU_BIAS epilogue)";
+      if (wl == TFORGE_MATMUL) kernel = a.math == "lt" ? "cublasLtMatmul(f32)" : "cublasLtMatmul(tf32)";
     } else {
-      die("--math default|tf32|bf16");
+      die("--math default|tf32|bf16|bf16x9|lt|lt_tf32");
     }
     run = [&, one, zero] {
-      if (a.math == "bf16") {
+      if (a.math == "lt" || a.math == "lt_tf32") {
+        blas_ok(cublasLtMatmul(lt, ltDesc, &one, dB, ltB, dA, ltA, &zero, dC, ltC, dC, ltC, &ltHeur.algo, ltWs,
+                               size_t(64) << 20, stream),
+                "cublasLtMatmul");
+        if (wl == TFORGE_MATMUL_ADD) add_inplace<<<(unsigned)((M * N + 255) / 256), 256, 0, stream>>>(dC, dRes, M * N);
+        cuda_ok(cudaGetLastError(), "epilogue launch");
+        return;
+      }
+      if (a.math == "bf16x9") {
+        blas_ok(cublasGemmEx(blas, CUBLAS_OP_N, CUBLAS_OP_N, (int)N, (int)M, (int)K, &one, dB, CUDA_R_32F, (int)N,
+                             dA, CUDA_R_32F, (int)K, &zero, dC, CUDA_R_32F, (int)N,
+                             CUBLAS_COMPUTE_32F_EMULATED_16BFX9, CUBLAS_GEMM_DEFAULT),
+                "cublasGemmEx(bf16x9)");
+      } else if (a.math == "bf16") {
         to_bf16<<<(unsigned)((M * K + 255) / 256), 256, 0, stream>>>(dA, abf, M * K);
         to_bf16<<<(unsigned)((K * N + 255) / 256), 256, 0, stream>>>(dB, bbf, K * N);
         blas_ok(cublasGemmEx(blas, CUBLAS_OP_N, CUBLAS_OP_N, (int)N, (int)M, (int)K, &one, bbf,
