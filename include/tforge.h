@@ -94,8 +94,8 @@ int tforge_gemm(const tforge_gemm_args *args, void *stream);
  * to the device, the launch, cudaMemcpy of C back (runners/gpu/tforge-gpu-bench.cu:198-207,
  * 292-302,327) -- with an overlapped one: device staging comes from the library's pool; B and
  * bias are copied first, then A (and C_res) in chunks of `chunk_rows` rows (0: automatic, at
- * most 8 chunks); each chunk's kernel starts on its own stream once its rows have landed,
- * and each chunk of out is copied back while later chunks compute.  Asynchronous with
+ * most 8 chunks of at least 512 rows); each chunk's kernel starts on its own stream once its
+ * rows have landed, and each chunk of out is copied back while later chunks compute.  Asynchronous with
  * respect to the host: out is complete once `stream` has synchronized.  Copies overlap only
  * with page-locked host memory; pageable memory gives the same results without overlap.
  * Results equal tforge_gemm's on each chunk of rows (the kernel is chosen per chunk). */

@@ -82,11 +82,12 @@ extern "C" int tforge_gemm_host(const tforge_gemm_args *a, int64_t chunk_rows, v
   const bool mbr = a->workload == TFORGE_MBR, add = a->workload == TFORGE_MATMUL_ADD;
   const bool b16 = a->mode == TFORGE_MODE_BF16 && a->b_dtype == TFORGE_F32 && K > 0 && N % 8 == 0;
 
-  // Rows per chunk: automatic = at most 8 chunks of a multiple of 128 rows (at least 256
-  // rows each); never more than 64 chunks.
+  // Rows per chunk: automatic = at most 8 chunks of a multiple of 128 rows, at least 512
+  // rows each (a chunk's kernel costs the whole K loop however few rows it has; 2048^3 on a
+  // B200: 512-row chunks 0.85 ms, 256-row 0.88, 1024-row 0.89); never more than 64 chunks.
   int64_t rows = chunk_rows;
   if (rows <= 0) {
-    const int64_t chunks = std::min(kAutoChunks, std::max<int64_t>(1, M / 256));
+    const int64_t chunks = std::min(kAutoChunks, std::max<int64_t>(1, M / 512));
     rows = ((M + chunks - 1) / chunks + 127) / 128 * 128;
   }
   rows = std::max(rows, (M + kMaxChunks - 1) / kMaxChunks);
