@@ -192,6 +192,24 @@ def test_runner_lib_and_cublas_modes(gpu, tmp_path):
         assert r["median_ms"] > 0
 
 
+@pytest.mark.parametrize("math,precision", [("default", "fp32"), ("bf16x9", "fp32"), ("lt", "fp32"),
+                                            ("lt_tf32", "tf32"), ("tf32", "tf32"), ("bf16", "bf16")])
+def test_runner_cublas_comparators_within_bound(gpu, tmp_path, math, precision):
+    """Every cuBLAS comparator path of the runner computes relu(A@B+bias) on the reference's
+    inputs within the bound of its precision (bf16x9 emulation and FP32 paths: the fp32
+    bound; TF32 and bf16 paths: their looser bounds)."""
+    m, n, k = 384, 512, 256
+    ins = tc.make_inputs("mbr", m, n, k, 1234)
+    for name, arr in ins.items():
+        arr.tofile(tmp_path / f"{name}.bin")
+    subprocess.run([str(tg.GPU_BENCH), "--mode", "cublas", "--math", math, "--workload", "mbr", "--m", str(m),
+                    "--n", str(n), "--k", str(k), "--warmup", "0", "--reps", "1", "--in-dir", str(tmp_path),
+                    "--out", str(tmp_path / "out.bin")], capture_output=True, text=True, check=True)
+    out = np.fromfile(tmp_path / "out.bin", dtype=np.float32).reshape(m, n)
+    res = tc.check_output("mbr", ins, out, precision)
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+
+
 def test_shim_check_matches_reference_api(gpu):
     """tg.check returns (res, out) like python/tforge_gpu.py:112-145, for lib and cuBLAS."""
     for mode in ("kernel", "cublas"):
