@@ -95,8 +95,8 @@ int tforge_gemm(const tforge_gemm_args *args, void *stream);
  * 292-302,327) -- with an overlapped one: device staging comes from the library's pool; B and
  * bias are copied first, then A (and C_res) in chunks of `chunk_rows` rows (0: automatic, at
  * most 8 chunks of at least 512 rows); each chunk's kernel starts on its own stream once its
- * rows have landed, and each chunk of out is copied back while later chunks compute.  Asynchronous with
- * respect to the host: out is complete once `stream` has synchronized.  Copies overlap only
+ * rows have landed, and each chunk of out is copied back while later chunks compute.
+ * Asynchronous with respect to the host: out is complete once `stream` has synchronized.  Copies overlap only
  * with page-locked host memory; pageable memory gives the same results without overlap.
  * Results equal tforge_gemm's on each chunk of rows (the kernel is chosen per chunk). */
 int tforge_gemm_host(const tforge_gemm_args *args, int64_t chunk_rows, void *stream);
@@ -161,7 +161,9 @@ typedef struct tforge_config {
   int32_t kernel;        /* 0 = table, 1 = tcgen05 one CTA per tile, 2 = SIMT, 3 = tcgen05 CTA pair */
   int32_t bn;            /* 64, 128 or 256 (one-CTA kernel) */
   int32_t stages;
-  int32_t persistent;
+  int32_t persistent;    /* reserved, 0 */
+  int32_t split_k;       /* CTA-pair kernel in fp32 / TF32 mode: 0 = automatic, 1 = no split,
+                            S = 2..8 pairs per tile, each over K / S */
 } tforge_config;
 
 int tforge_set_config(const tforge_config *cfg);

@@ -303,6 +303,37 @@ bool tma_compatible(const tforge_gemm_args *a, int64_t lda, int64_t ldb, int64_t
   return true;
 }
 
+// SM pairs of the current device (148 SMs on a B200 when no device is visible).
+int device_pairs() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    return 74;
+  }
+  return sms / 2;
+}
+
+// Split-K factor of the CTA-pair kernel: tforge_config.split_k when set, else (fp32 and TF32
+// modes) as many pairs per tile as fit one wave of SM pairs, at most 8 and at least 4
+// k-blocks each; BF16 never splits (so the allocation-free BF16 entry matches it).
+int pair_splits(const TcConfig &c, int64_t M, int64_t N, int64_t K) {
+  if (!c.pair) return 1;
+  {
+    std::lock_guard<std::mutex> lk(g_cfg_mu);
+    if (g_cfg.kernel == 3 && g_cfg.split_k > 0) return g_cfg.split_k;
+  }
+  if (c.prec == PREC_BF16) return 1;
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t kb = (K + 31) / 32;
+  const int64_t pairs = device_pairs();
+  if (tiles * 2 > pairs) return 1;
+  int64_t sk = pairs / tiles;
+  if (sk > kb / 4) sk = kb / 4;
+  if (sk > 8) sk = 8;
+  return sk >= 2 ? (int)sk : 1;
+}
+
 int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const void *B,
            bool bf16, int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t st) {
   const int esz = bf16 ? 2 : 4;
@@ -326,7 +357,32 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   p.debug_skip = g_debug_skip.load();
   const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
   cudaError_t e;
-  if (cfg.pair) {
+  const int splits = pair_splits(cfg, a->M, a->N, a->K);
+  if (cfg.pair && splits > 1) {
+    // Split-K: raw partial sums of each k-range into slice z of a pooled workspace (rows
+    // padded to whole tiles so no tile crosses a slice), then one pass sums the slices in
+    // order and applies the epilogue.
+    const int64_t mp = (a->M + 255) / 256 * 256;
+    cudaMemPool_t pool = nullptr;
+    rc = scratch_pool(&pool);
+    if (rc) return rc;
+    void *ws = nullptr;
+    cudaError_t e2 = cudaMallocFromPoolAsync(&ws, sizeof(float) * (size_t)splits * mp * a->N, pool, st);
+    if (e2 != cudaSuccess) return cuda_fail(e2, "cudaMallocFromPoolAsync(split-K workspace)");
+    CUtensorMap tmW;
+    rc = make_tmap(&tmW, ws, false, splits * mp, a->N, a->N, 32, 128);
+    if (rc) {
+      cudaFreeAsync(ws, st);
+      return rc;
+    }
+    p.splits = splits;
+    p.split_rows = (int32_t)mp;
+    e = launch_gemm_pair(cfg.prec, cfg.stages, EPI_MATMUL, tmA, tmB, tmW, tmW, p, st);
+    if (e == cudaSuccess)
+      e = launch_splitk_reduce(epi, static_cast<const float *>(ws), splits, mp * a->N, a->M, a->N, a->bias, a->C_res,
+                               a->out, ldc, st);
+    cudaFreeAsync(ws, st);
+  } else if (cfg.pair) {
     CUtensorMap tmO, tmC;
     rc = make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 32, 128);
     if (rc) return rc;
@@ -556,6 +612,8 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
   out->grid[1] = (int)((M + tm - 1) / tm);
   out->grid[2] = 1;
   out->block[0] = c.tc.pair && c.tc.prec == PREC_X3 ? 384 : 256;  // 3xTF32 pair: 12 warps
+  out->split_k = pair_splits(c.tc, M, N, K);
+  out->grid[2] = out->split_k;
   out->block[1] = out->block[2] = 1;
   out->cluster[0] = c.tc.pair ? 2 : 1;
   out->smem_bytes = c.tc.pair ? pair_smem_bytes(c.tc.prec, c.tc.stages) : tc_smem_bytes(c.tc);
@@ -580,7 +638,7 @@ int tforge_set_config(const tforge_config *cfg) {
     g_cfg = tforge_config{};
     return TFORGE_OK;
   }
-  if (cfg->kernel < 0 || cfg->kernel > 3) return TFORGE_ERR_MODE;
+  if (cfg->kernel < 0 || cfg->kernel > 3 || cfg->split_k < 0 || cfg->split_k > 8) return TFORGE_ERR_MODE;
   g_cfg = *cfg;
   return TFORGE_OK;
 }

@@ -186,7 +186,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int n0 = (blockIdx.x >> 1) * 256, m0 = blockIdx.y * 256 + (int)rank * 128;
-  const int nkb = (p.K + L::kBK - 1) / L::kBK;
+  // Split-K: this pair takes k-blocks [kb0, kb0 + nkb) of the tile's K and stores raw
+  // partial sums at row offset blockIdx.z * split_rows of the output map.
+  const int nkb_all = (p.K + L::kBK - 1) / L::kBK;
+  const int splits = p.splits > 1 ? p.splits : 1;
+  const int kb0 = (int)((int64_t)blockIdx.z * nkb_all / splits);
+  const int nkb = (int)((int64_t)(blockIdx.z + 1) * nkb_all / splits) - kb0;
+  const int out_row0 = m0 + (int)blockIdx.z * p.split_rows;
   const WaitCtl wc{abort_flag, p.status, p.limit_ns};
 
   if (threadIdx.x == 0) {
@@ -234,7 +240,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         if (!ok) break;
       }
       if (p.debug_skip && kb == 0) continue;  // test hook: this stage never fills
-      const int kc = kb * L::kBK;
+      const int kc = (kb0 + kb) * L::kBK;
       const int nb = n0 + (int)rank * L::kBNHalf;
       if constexpr (kX3) {
         mbar_arrive_expect_tx(full0 + 8 * s, L::kStageBytes);
@@ -439,7 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         fence_proxy_async_smem();
         named_barrier(1 + c, 128);
         if (q == 0 && lane == 0 && res_ok && cta_rows && col0 < p.N) {
-          tma_store_2d(&tmO, sbase + c * L::kEpiBoxBytes, col0, m0);
+          tma_store_2d(&tmO, sbase + c * L::kEpiBoxBytes, col0, out_row0);
           bulk_commit_group();
         }
       }
@@ -470,7 +476,7 @@ cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, cons
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
-  dim3 grid(2 * ((p.N + 255) / 256), (p.M + 255) / 256, 1);
+  dim3 grid(2 * ((p.N + 255) / 256), (p.M + 255) / 256, p.splits > 1 ? p.splits : 1);
   kern<<<grid, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, tmO, tmC, p);
   return cudaGetLastError();
 }

@@ -29,6 +29,11 @@ struct TcParams {
   uint32_t *status;    // device status word
   uint64_t limit_ns;   // bounded-wait limit
   int32_t debug_skip;  // test hook: skip the first stage's loads
+  // Split-K (CTA-pair kernel): `splits` > 1 CTA pairs per tile (grid z) each take an equal
+  // k-range and store raw partial sums into slice z of the output map, at row offset
+  // z * split_rows; 0 or 1 = no split.
+  int32_t splits;
+  int32_t split_rows;
 };
 
 struct TcConfig {
@@ -84,5 +89,10 @@ void simt_launch_shape(int64_t M, int64_t N, int grid[3], int block[3], int *sme
 cudaError_t launch_elementwise(int op, const float *X, const float *Y, float *Z, int64_t M,
                                int64_t N, cudaStream_t stream);
 cudaError_t launch_convert_bf16(const float *x, uint16_t *y, int64_t n, cudaStream_t stream);
+// Split-K epilogue: out[m, n] = epi(sum over s = 0..S-1, in order, of ws[s * slice + m * N + n]);
+// N a multiple of 4, 16-byte-aligned rows.
+cudaError_t launch_splitk_reduce(int epi, const float *ws, int splits, int64_t slice, int64_t M, int64_t N,
+                                 const float *bias, const float *cres, float *out, int64_t ldc,
+                                 cudaStream_t stream);
 
 }  // namespace tf

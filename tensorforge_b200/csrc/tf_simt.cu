@@ -204,3 +204,56 @@ cudaError_t launch_convert_bf16(const float *x, uint16_t *y, int64_t n, cudaStre
 }
 
 }  // namespace tf
+
+namespace tf {
+namespace {
+
+// Split-K epilogue, one float4 per thread step: the S partial sums in slice order, then the
+// operator's epilogue (one IEEE add for bias / C_res, IEEE maximum for relu).
+__global__ void splitk_reduce_kernel(int epi, const float4 *__restrict__ ws, int splits, int64_t slice4, int64_t M,
+                                     int64_t n4, const float4 *__restrict__ bias, const float *__restrict__ cres,
+                                     float *__restrict__ out, int64_t ldc) {
+  const int64_t total = M * n4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / n4, c = i - m * n4;
+    float4 acc = ws[i];
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = ws[s * slice4 + i];
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    if (epi == EPI_MBR) {
+      const float4 b = bias[c];
+      acc.x = relu_max(__fadd_rn(acc.x, b.x));
+      acc.y = relu_max(__fadd_rn(acc.y, b.y));
+      acc.z = relu_max(__fadd_rn(acc.z, b.z));
+      acc.w = relu_max(__fadd_rn(acc.w, b.w));
+    } else if (epi == EPI_ADD) {
+      const float4 r = *reinterpret_cast<const float4 *>(cres + m * ldc + 4 * c);
+      acc.x = __fadd_rn(acc.x, r.x);
+      acc.y = __fadd_rn(acc.y, r.y);
+      acc.z = __fadd_rn(acc.z, r.z);
+      acc.w = __fadd_rn(acc.w, r.w);
+    }
+    *reinterpret_cast<float4 *>(out + m * ldc + 4 * c) = acc;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_splitk_reduce(int epi, const float *ws, int splits, int64_t slice, int64_t M, int64_t N,
+                                 const float *bias, const float *cres, float *out, int64_t ldc,
+                                 cudaStream_t stream) {
+  const int64_t n4 = N / 4, total = M * n4;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, stream>>>(epi, reinterpret_cast<const float4 *>(ws), splits,
+                                                             slice / 4, M, n4, reinterpret_cast<const float4 *>(bias),
+                                                             cres, out, ldc);
+  return cudaGetLastError();
+}
+
+}  // namespace tf

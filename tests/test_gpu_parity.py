@@ -192,6 +192,37 @@ def test_runner_lib_and_cublas_modes(gpu, tmp_path):
         assert r["median_ms"] > 0
 
 
+@pytest.mark.parametrize("splits", [2, 3, 8])
+@pytest.mark.parametrize("mode", ["fp32", "tf32"])
+@pytest.mark.parametrize("workload", ["mbr", "matmul", "matmul_add"])
+@pytest.mark.parametrize("shape", [(300, 264, 1024), (512, 512, 2048)], ids=lambda s: "x".join(map(str, s)))
+def test_pair_split_k_within_bound_and_deterministic(gpu, workload, mode, splits, shape):
+    """Split-K on the pair kernel: S pairs per tile over K / S each, partial sums summed in a
+    fixed order; ragged M and N, every epilogue; two runs agree bit for bit."""
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 21)
+    _lib.set_config(3, split_k=splits)
+    try:
+        assert _lib.describe(workload, m, n, k, mode)["split_k"] == splits
+        out = tg.run_op(workload, ins, m, n, k, mode)
+        again = tg.run_op(workload, ins, m, n, k, mode)
+    finally:
+        _lib.set_config()
+    assert np.array_equal(bits(out), bits(again))
+    res = tc.check_output(workload, ins, out, mode)
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+
+
+def test_automatic_split_k_small_square(gpu):
+    """1024^3 has 16 pair tiles for 74 SM pairs: the dispatch splits K and stays in bound."""
+    d = _lib.describe("mbr", 1024, 1024, 1024, "fp32")
+    assert d["kernel"].endswith("_pair") and d["split_k"] >= 2 and d["grid"][2] == d["split_k"]
+    ins = tc.make_inputs("mbr", 1024, 1024, 1024, 5)
+    out = tg.run_op("mbr", ins, 1024, 1024, 1024, "fp32")
+    res = tc.check_output("mbr", ins, out, "fp32")
+    assert res["err_over_bound"] <= 1.0, res
+
+
 @pytest.mark.parametrize("math,precision", [("default", "fp32"), ("bf16x9", "fp32"), ("lt", "fp32"),
                                             ("lt_tf32", "tf32"), ("tf32", "tf32"), ("bf16", "bf16")])
 def test_runner_cublas_comparators_within_bound(gpu, tmp_path, math, precision):
