@@ -58,7 +58,7 @@ def test_config1_fp32_mode(gpu, seed):
     """relu(x @ w + b), x 256x128, w 128x256, seeds 0 and 1234."""
     ins = tc.make_inputs("mbr", 256, 256, 128, seed)
     d = _lib.describe("mbr", 256, 256, 128, "fp32")
-    assert d["kernel"] == "tf_gemm_tcgen05_3xtf32_pair"  # the tuning sweep's winner at this shape
+    assert d["kernel"].startswith("tf_gemm_tcgen05_3xtf32")  # whichever 3xTF32 kernel the sweep measured fastest
     out = tg.run_op("mbr", ins, 256, 256, 128, "fp32")
     res = tc.check_output("mbr", ins, out)
     assert res["pass"] and res["err_over_bound"] < 0.25, res
