@@ -303,7 +303,12 @@ def ours(args):
             bias.uniform_(-1, 1, generator=g0)
     bcast_ms = None
     if world > 1:
-        dist.barrier()  # communicator set-up is not part of the broadcast time
+        # Communicator and broadcast-channel set-up are not part of the broadcast time: one
+        # small broadcast first (NCCL connects a collective's channels on its first use).
+        dist.barrier()
+        warm = torch.zeros(1 << 18, device=dev)
+        dist.broadcast(warm, 0)
+        del warm
     torch.cuda.synchronize()
     # Once per weight set, outside the timed region; timed with CUDA events on this rank's
     # stream (the collective's completion is ordered before the second event), max over ranks.
