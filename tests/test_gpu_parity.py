@@ -364,3 +364,43 @@ def test_mlp_chain_per_layer_bound(gpu, mode):
     r1 = tc.check_output("mbr", {"a": ins["x"], "b": ins["w1"], "bias": ins["b1"]}, hn, mode)
     r2 = tc.check_output("mbr", {"a": hn, "b": ins["w2"], "bias": ins["b2"]}, on, mode)
     assert r1["pass"] and r2["pass"], (r1, r2)
+
+
+def test_concurrent_streams_match_single_stream(gpu):
+    """Calls interleaved on two streams (split-K workspace and bf16 scratch come from the
+    stream-ordered pool) give the same bits as the same calls on one stream."""
+    import torch
+
+    cases = [("mbr", (1024, 1024, 1024), "fp32"),   # split-K: pooled workspace
+             ("mbr", (512, 384, 256), "bf16"),      # bf16 operand scratch from the pool
+             ("matmul_add", (2048, 1024, 512), "tf32")]
+    dev = torch.device("cuda", 0)
+    data = []
+    for wl, (m, n, k), mode in cases:
+        ins = tc.make_inputs(wl, m, n, k, 77)
+        t = {name: torch.from_numpy(arr).to(dev) for name, arr in ins.items()}
+        data.append((wl, m, n, k, mode, t))
+
+    def launch(i, stream, out):
+        wl, m, n, k, mode, t = data[i]
+        _lib.gemm(wl, t["a"].data_ptr(), t["b"].data_ptr(), out.data_ptr(), m, n, k, mode,
+                  bias=t["bias"].data_ptr() if "bias" in t else None,
+                  c_res=t["c"].data_ptr() if "c" in t else None, stream=stream.cuda_stream)
+
+    ref = []
+    s0 = torch.cuda.Stream()
+    for i, (wl, m, n, k, mode, t) in enumerate(data):
+        out = torch.empty((m, n), device=dev)
+        launch(i, s0, out)
+        ref.append(out)
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [[torch.full((m, n), float("nan"), device=dev) for (_, m, n, _, _, _) in data] for _ in range(4)]
+    for r in range(4):
+        for i in range(len(data)):
+            launch(i, streams[(r + i) % 2], outs[r][i])
+    torch.cuda.synchronize()
+    assert _lib.device_status(None) == _lib.OK
+    for r in range(4):
+        for i in range(len(data)):
+            assert torch.equal(outs[r][i].view(torch.int32), ref[i].view(torch.int32)), (r, data[i][:5])
