@@ -89,11 +89,14 @@ struct PairLayout {
   static constexpr int kRingBytes = kLand * kStageBytes + kOps * kOpBytes;
   // Barriers: full[kLand], lempty[kLand] (3xTF32: converters -> producer), conv[kOps],
   // ready[kOps], empty[kOps] (MMA commit), accf, resf.
-  static constexpr int kNumBars = 2 * kLand + 3 * kOps + 2;
+  static constexpr int kNumBars = 2 * kLand + 3 * kOps + 3;
   // barriers, then tmem slot, abort flag, epilogue flag, spare, and one mailbox word per
   // operand stage (the peer's st.async tokens land there).
   static constexpr int kBarBytes = 8 * kNumBars + 16 + 4 * kOps;
-  static constexpr int kSmemBytes = 1024 + kRingBytes + kBarBytes;
+  // The tile's 256 bias values, staged during the mainloop for the epilogue.
+  static constexpr int kBiasBytes = 256 * 4;
+  __host__ __device__ static constexpr int bias_off() { return kRingBytes + (kBarBytes + 15) / 16 * 16; }
+  static constexpr int kSmemBytes = 1024 + kRingBytes + (kBarBytes + 15) / 16 * 16 + kBiasBytes;
   static constexpr uint32_t kAccCols = 256;
   static constexpr uint32_t kTmemCols = kX3 ? 512u : 256u;
   static constexpr int kConvWarps = 10;                // warps 2..11 (3xTF32)
@@ -175,10 +178,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   // leader's barrier counts both CTAs' bytes); lempty[l] (3xTF32): this CTA's converters
   // have loaded slot l; conv[o]: this CTA's converters filled operand slot o; ready[o]
   // (leader): the peer's converters did; empty[o]: the pair MMAs reading operand slot o
-  // are done (TF32/BF16: operand slot = landing slot); accf: accumulator done.
+  // are done (TF32/BF16: operand slot = landing slot); accf: accumulator done; resf: C_res
+  // boxes landed; biasf: the tile's bias is staged in shared memory.
   constexpr int kL = L::kLand, kO = L::kOps;
   const uint32_t full0 = smem_u32(bars), lempty0 = full0 + 8 * kL, conv0 = lempty0 + 8 * kL,
-                 ready0 = conv0 + 8 * kO, empty0 = ready0 + 8 * kO, accf = empty0 + 8 * kO, resf = accf + 8;
+                 ready0 = conv0 + 8 * kO, empty0 = ready0 + 8 * kO, accf = empty0 + 8 * kO, resf = accf + 8,
+                 biasf = resf + 8;
+  float4 *bias_s = reinterpret_cast<float4 *>(smem + L::bias_off());
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
   volatile uint32_t *abort_flag = tmem_slot + 1;
   const uint32_t mailbox0 = smem_u32(tmem_slot + 4);
@@ -207,6 +213,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
     }
     mbar_init(accf, 1);
     mbar_init(resf, 1);
+    mbar_init(biasf, 2);  // warps 2 and 3
     *abort_flag = 0u;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -223,6 +230,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   cluster_sync();  // the peer's barriers are initialised before any remote arrive or TMA
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  if constexpr (EPI == EPI_MBR) {
+    // Warps 2 and 3 stage this tile's 256 bias values (64 float4; N is a multiple of 4 and
+    // bias 16-byte aligned on this path) while the first loads are in flight, so the
+    // epilogue reads bias from shared memory instead of waiting on global loads per chunk.
+    if (warp == 2 || warp == 3) {
+      const int i = threadIdx.x - 64, col = n0 + 4 * i;
+      bias_s[i] = col < p.N ? __ldg(reinterpret_cast<const float4 *>(p.bias + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(biasf);
+    }
+  }
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -392,7 +411,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
     // waiting for a warp that gave up.
     constexpr int kEpiThreads = 32 * L::kEpiWarps;
     volatile uint32_t *epi_ok = tmem_slot + 2;
-    if (warp == 4 && lane == 0) *epi_ok = mbar_wait_cluster(accf, 0, wc, 128) ? 1u : 0u;
+    if (warp == 4 && lane == 0)
+      *epi_ok = (mbar_wait_cluster(accf, 0, wc, 128) && (EPI != EPI_MBR || mbar_wait(biasf, 0, wc))) ? 1u : 0u;
     named_barrier(9, kEpiThreads);
     if (*epi_ok) {
       tc_fence_after();
@@ -425,9 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
                                    __uint_as_float(rr[4 * j + 2]), __uint_as_float(rr[4 * j + 3]));
             float4 *slot = reinterpret_cast<float4 *>(box + ((j ^ (r & 7)) << 4));
             if constexpr (EPI == EPI_MBR) {
-              const int col = col0 + 4 * j;
-              const float4 b = col < p.N ? __ldg(reinterpret_cast<const float4 *>(p.bias + col))
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float4 b = bias_s[c * 8 + j];  // bias of columns col0 + 4 j .. + 3
               v.x = relu_ieee(__fadd_rn(v.x, b.x));
               v.y = relu_ieee(__fadd_rn(v.y, b.y));
               v.z = relu_ieee(__fadd_rn(v.z, b.z));
