@@ -30,15 +30,23 @@ __device__ __forceinline__ float relu_max(float x) {
   return __uint_as_float(keep ? u : 0u);
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(256) gemm_simt_kernel(const float *__restrict__ A,
-                                                        const float *__restrict__ B,
-                                                        const float *__restrict__ aux,
-                                                        float *__restrict__ C, int64_t M, int64_t N,
-                                                        int64_t K, int64_t lda, int64_t ldb,
-                                                        int64_t ldc) {
-  __shared__ float As[2][SBK][SBM];
-  __shared__ float Bs[2][SBK][SBN];
+// Thread (tx, ty) = (tid % 16, tid / 16) owns rows {4 ty + i, 64 + 4 ty + i} and columns
+// {4 tx + j, 64 + 4 tx + j} (i, j < 4) of the 128x128 tile: per k it reads two float4 of A and
+// two of B from shared memory for 64 FMAs.  Every output keeps one accumulator updated by one
+// fmaf per k in increasing k from +0.0, so the result is the reference's bit for bit.  The next
+// K tile is fetched into registers while this one is consumed (float4 global loads when the
+// pointers and pitches allow, VEC), then stored into the other shared-memory buffer.
+template <int EPI, bool VEC>
+__global__ void __launch_bounds__(256, 2) gemm_simt_kernel(const float *__restrict__ A,
+                                                           const float *__restrict__ B,
+                                                           const float *__restrict__ aux,
+                                                           float *__restrict__ C, int64_t M, int64_t N,
+                                                           int64_t K, int64_t lda, int64_t ldb,
+                                                           int64_t ldc) {
+  // A tile transposed (As[k][m]); 4 floats of padding put the two k halves a thread group
+  // stores into different banks, and keep every row 16-byte aligned.
+  __shared__ __align__(16) float As[2][SBK][SBM + 4];
+  __shared__ __align__(16) float Bs[2][SBK][SBN];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t m0 = (int64_t)blockIdx.y * SBM, n0 = (int64_t)blockIdx.x * SBN;
   float acc[STM][STN];
@@ -47,60 +55,94 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const float *__restrict_
 #pragma unroll
     for (int j = 0; j < STN; ++j) acc[i][j] = 0.0f;
 
-  // Each thread stages 4 elements of A (column k = tid % 8, rows tid / 8 + 32 i) and
-  // 4 of B (row k = tid / 32, columns tid % 32 + 32 j) per K tile.
-  auto load = [&](int buf, int64_t k0) {
-    const int ak = tid & 7, ar = tid >> 3;
+  // Staging of one K tile: A row ar = tid / 2, k (tid % 2) * 4 .. +3; B row bk = tid / 32,
+  // columns (tid % 32) * 4 .. +3.  Out-of-range elements read as 0.
+  const int ar = tid >> 1, ak = (tid & 1) * 4, bk = tid >> 5, bc = (tid & 31) * 4;
+  float ra[4], rb[4];
+  auto gload = [&](int64_t k0) {
+    const int64_t m = m0 + ar, k = k0 + ak;
+    if (VEC && m < M && k + 3 < K) {
+      const float4 v = __ldg(reinterpret_cast<const float4 *>(A + m * lda + k));
+      ra[0] = v.x; ra[1] = v.y; ra[2] = v.z; ra[3] = v.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t m = m0 + ar + 32 * i, k = k0 + ak;
-      As[buf][ak][ar + 32 * i] = (m < M && k < K) ? A[m * lda + k] : 0.0f;
+      for (int c = 0; c < 4; ++c) ra[c] = (m < M && k + c < K) ? __ldg(A + m * lda + k + c) : 0.0f;
     }
-    const int bk = tid >> 5, bc = tid & 31;
+    const int64_t kb = k0 + bk, n = n0 + bc;
+    if (VEC && kb < K && n + 3 < N) {
+      const float4 v = __ldg(reinterpret_cast<const float4 *>(B + kb * ldb + n));
+      rb[0] = v.x; rb[1] = v.y; rb[2] = v.z; rb[3] = v.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int64_t k = k0 + bk, n = n0 + bc + 32 * j;
-      Bs[buf][bk][bc + 32 * j] = (k < K && n < N) ? B[k * ldb + n] : 0.0f;
+      for (int c = 0; c < 4; ++c) rb[c] = (kb < K && n + c < N) ? __ldg(B + kb * ldb + n + c) : 0.0f;
     }
+  };
+  auto sstore = [&](int buf) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) As[buf][ak + c][ar] = ra[c];
+    *reinterpret_cast<float4 *>(&Bs[buf][bk][bc]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+  };
+  auto step = [&](int buf, int kk) {
+    const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][4 * ty]);
+    const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + 4 * ty]);
+    const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][4 * tx]);
+    const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][64 + 4 * tx]);
+    const float a[STM] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float b[STN] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int i = 0; i < STM; ++i)
+#pragma unroll
+      for (int j = 0; j < STN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
   };
 
   const int64_t ntiles = (K + SBK - 1) / SBK;
-  if (ntiles > 0) load(0, 0);
+  if (ntiles > 0) {
+    gload(0);
+    sstore(0);
+  }
   __syncthreads();
   for (int64_t t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < ntiles) load(buf ^ 1, (t + 1) * SBK);
-    const int64_t kleft = K - t * SBK;
-    const int kmax = kleft < SBK ? (int)kleft : SBK;  // never add a padded 0*0: -0 must stay -0
+    const int buf = (int)(t & 1);
+    const bool more = t + 1 < ntiles;
+    if (more) gload((t + 1) * SBK);
+    if (more || K - t * SBK == SBK) {
 #pragma unroll
-    for (int kk = 0; kk < SBK; ++kk) {
-      if (kk < kmax) {
-        float a[STM], b[STN];
+      for (int kk = 0; kk < SBK; ++kk) step(buf, kk);
+    } else {
+      // Last, partial tile: never add a padded 0 * 0 (-0 must stay -0).
+      const int kmax = (int)(K - t * SBK);
 #pragma unroll
-        for (int i = 0; i < STM; ++i) a[i] = As[buf][kk][ty + 16 * i];
-#pragma unroll
-        for (int j = 0; j < STN; ++j) b[j] = Bs[buf][kk][tx + 16 * j];
-#pragma unroll
-        for (int i = 0; i < STM; ++i)
-#pragma unroll
-          for (int j = 0; j < STN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-      }
+      for (int kk = 0; kk < SBK; ++kk)
+        if (kk < kmax) step(buf, kk);
     }
+    if (more) sstore(buf ^ 1);
     __syncthreads();
   }
 
 #pragma unroll
   for (int i = 0; i < STM; ++i) {
-    const int64_t m = m0 + ty + 16 * i;
+    const int64_t m = m0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + (i - 4));
     if (m >= M) continue;
 #pragma unroll
-    for (int j = 0; j < STN; ++j) {
-      const int64_t n = n0 + tx + 16 * j;
-      if (n >= N) continue;
-      float v = acc[i][j];
-      if (EPI == EPI_MBR) v = relu_max(__fadd_rn(v, aux[n]));
-      else if (EPI == EPI_ADD) v = __fadd_rn(v, aux[m * ldc + n]);
-      C[m * ldc + n] = v;
+    for (int jh = 0; jh < 2; ++jh) {
+      const int64_t n = n0 + 64 * jh + 4 * tx;
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t nn = n + j;
+        v[j] = acc[i][4 * jh + j];
+        if (nn < N) {
+          if (EPI == EPI_MBR) v[j] = relu_max(__fadd_rn(v[j], aux[nn]));
+          else if (EPI == EPI_ADD) v[j] = __fadd_rn(v[j], aux[m * ldc + nn]);
+        }
+      }
+      if (VEC && n + 3 < N) {
+        *reinterpret_cast<float4 *>(C + m * ldc + n) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n + j < N) C[m * ldc + n + j] = v[j];
+      }
     }
   }
 }
@@ -156,24 +198,38 @@ void simt_launch_shape(int64_t M, int64_t N, int grid[3], int block[3], int *sme
   *smem = 0;
 }
 
+// Float4 global access needs 16-byte-aligned bases and pitches (C_res shares ldc).
+static bool simt_vec_ok(const float *A, const float *B, const float *aux, const float *C, int64_t lda, int64_t ldb,
+                        int64_t ldc, int epi) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return lda % 4 == 0 && ldb % 4 == 0 && ldc % 4 == 0 && al(A) && al(B) && al(C) &&
+         (epi != EPI_ADD || al(aux));
+}
+
+template <int EPI>
+static void launch_simt_epi(bool vec, dim3 grid, cudaStream_t stream, const float *A, const float *B,
+                            const float *aux, float *C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                            int64_t ldc) {
+  if (vec) gemm_simt_kernel<EPI, true><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
+  else gemm_simt_kernel<EPI, false><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
+}
+
 cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const float *aux, float *C,
                              int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                              int64_t ldc, cudaStream_t stream) {
   if (M == 0 || N == 0) return cudaSuccess;
   dim3 grid((unsigned)((N + SBN - 1) / SBN), (unsigned)((M + SBM - 1) / SBM));
-  if (epi == EPI_MATMUL)
-    gemm_simt_kernel<EPI_MATMUL><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
-  else if (epi == EPI_MBR)
-    gemm_simt_kernel<EPI_MBR><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
-  else
-    gemm_simt_kernel<EPI_ADD><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
+  const bool vec = simt_vec_ok(A, B, aux, C, lda, ldb, ldc, epi);
+  if (epi == EPI_MATMUL) launch_simt_epi<EPI_MATMUL>(vec, grid, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
+  else if (epi == EPI_MBR) launch_simt_epi<EPI_MBR>(vec, grid, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
+  else launch_simt_epi<EPI_ADD>(vec, grid, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
   return cudaGetLastError();
 }
 
 cudaError_t simt_func_attributes(int epi, cudaFuncAttributes *a, int *blocks) {
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MBR>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_ADD>)
-                                   : reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MATMUL>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MBR, true>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_ADD, true>)
+                                   : reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MATMUL, true>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, f, 256, 0);
