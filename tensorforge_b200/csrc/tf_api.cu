@@ -592,8 +592,7 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
     int smem = 0;
     simt_launch_shape(M, N, out->grid, out->block, &smem);
     out->smem_bytes = smem;
-    out->tile[0] = 128;
-    out->tile[1] = 128;
+    out->tile[0] = out->tile[1] = simt_tile_size(M, N);
     out->tile[2] = 8;
     out->stages = 2;
     out->mode = TFORGE_MODE_FP32_EXACT;

@@ -84,6 +84,7 @@ cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const floa
                              int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                              int64_t ldc, cudaStream_t stream);
 void simt_launch_shape(int64_t M, int64_t N, int grid[3], int block[3], int *smem);
+int simt_tile_size(int64_t M, int64_t N);  // 128 or 64 (square tiles)
 
 // Elementwise ops: op 0 add, 1 relu, 2 bias_add.
 cudaError_t launch_elementwise(int op, const float *X, const float *Y, float *Z, int64_t M,

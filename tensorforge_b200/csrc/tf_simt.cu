@@ -30,69 +30,86 @@ __device__ __forceinline__ float relu_max(float x) {
   return __uint_as_float(keep ? u : 0u);
 }
 
-// Thread (tx, ty) = (tid % 16, tid / 16) owns rows {4 ty + i, 64 + 4 ty + i} and columns
-// {4 tx + j, 64 + 4 tx + j} (i, j < 4) of the 128x128 tile: per k it reads two float4 of A and
-// two of B from shared memory for 64 FMAs.  Every output keeps one accumulator updated by one
-// fmaf per k in increasing k from +0.0, so the result is the reference's bit for bit.  The next
-// K tile is fetched into registers while this one is consumed (float4 global loads when the
-// pointers and pitches allow, VEC), then stored into the other shared-memory buffer.
-template <int EPI, bool VEC>
-__global__ void __launch_bounds__(256, 2) gemm_simt_kernel(const float *__restrict__ A,
-                                                           const float *__restrict__ B,
-                                                           const float *__restrict__ aux,
-                                                           float *__restrict__ C, int64_t M, int64_t N,
-                                                           int64_t K, int64_t lda, int64_t ldb,
-                                                           int64_t ldc) {
-  // A tile transposed (As[k][m]); 4 floats of padding put the two k halves a thread group
+// BM x BN tile (128 or 64 each) on 256 threads.  Thread (tx, ty) = (tid % 16, tid / 16) owns
+// rows 64 h + 4 ty + i and columns 64 g + 4 tx + j (h < BM / 64, g < BN / 64, i, j < 4): per k
+// it reads BM / 64 float4 of A and BN / 64 of B from shared memory (128x128: 4 loads for 64
+// FMAs).  Every output keeps one accumulator updated by one fmaf per k in increasing k from
+// +0.0, so the result is the reference's bit for bit.  The next K tile is fetched into
+// registers while this one is consumed (vector global loads when the pointers and pitches
+// allow, VEC), then stored into the other shared-memory buffer.
+template <int EPI, bool VEC, int BM, int BN>
+__global__ void __launch_bounds__(256, BM == 128 ? 2 : 4) gemm_simt_kernel(
+    const float *__restrict__ A, const float *__restrict__ B, const float *__restrict__ aux, float *__restrict__ C,
+    int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc) {
+  constexpr int HM = BM / 64, HN = BN / 64;
+  constexpr int EA = BM / 32, EB = BN / 32;  // elements each thread stages per K tile
+  constexpr int TPR = SBK / EA;              // threads per A row
+  // A tile transposed (As[k][m]); 4 floats of padding put the k sub-rows a thread group
   // stores into different banks, and keep every row 16-byte aligned.
-  __shared__ __align__(16) float As[2][SBK][SBM + 4];
-  __shared__ __align__(16) float Bs[2][SBK][SBN];
+  __shared__ __align__(16) float As[2][SBK][BM + 4];
+  __shared__ __align__(16) float Bs[2][SBK][BN];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int64_t m0 = (int64_t)blockIdx.y * SBM, n0 = (int64_t)blockIdx.x * SBN;
-  float acc[STM][STN];
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  float acc[4 * HM][4 * HN];
 #pragma unroll
-  for (int i = 0; i < STM; ++i)
+  for (int i = 0; i < 4 * HM; ++i)
 #pragma unroll
-    for (int j = 0; j < STN; ++j) acc[i][j] = 0.0f;
+    for (int j = 0; j < 4 * HN; ++j) acc[i][j] = 0.0f;
 
-  // Staging of one K tile: A row ar = tid / 2, k (tid % 2) * 4 .. +3; B row bk = tid / 32,
-  // columns (tid % 32) * 4 .. +3.  Out-of-range elements read as 0.
-  const int ar = tid >> 1, ak = (tid & 1) * 4, bk = tid >> 5, bc = (tid & 31) * 4;
-  float ra[4], rb[4];
+  // Staging of one K tile: A row ar, k ak .. ak + EA - 1; B row bk, columns bc .. bc + EB - 1.
+  // Out-of-range elements read as 0.
+  const int ar = tid / TPR, ak = (tid % TPR) * EA, bk = tid >> 5, bc = (tid & 31) * EB;
+  float ra[EA], rb[EB];
   auto gload = [&](int64_t k0) {
     const int64_t m = m0 + ar, k = k0 + ak;
-    if (VEC && m < M && k + 3 < K) {
-      const float4 v = __ldg(reinterpret_cast<const float4 *>(A + m * lda + k));
-      ra[0] = v.x; ra[1] = v.y; ra[2] = v.z; ra[3] = v.w;
+    if (VEC && m < M && k + EA - 1 < K) {
+      if constexpr (EA == 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(A + m * lda + k));
+        ra[0] = v.x; ra[1] = v.y; ra[2] = v.z; ra[3] = v.w;
+      } else {
+        const float2 v = __ldg(reinterpret_cast<const float2 *>(A + m * lda + k));
+        ra[0] = v.x; ra[1] = v.y;
+      }
     } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) ra[c] = (m < M && k + c < K) ? __ldg(A + m * lda + k + c) : 0.0f;
+      for (int c = 0; c < EA; ++c) ra[c] = (m < M && k + c < K) ? __ldg(A + m * lda + k + c) : 0.0f;
     }
     const int64_t kb = k0 + bk, n = n0 + bc;
-    if (VEC && kb < K && n + 3 < N) {
-      const float4 v = __ldg(reinterpret_cast<const float4 *>(B + kb * ldb + n));
-      rb[0] = v.x; rb[1] = v.y; rb[2] = v.z; rb[3] = v.w;
+    if (VEC && kb < K && n + EB - 1 < N) {
+      if constexpr (EB == 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(B + kb * ldb + n));
+        rb[0] = v.x; rb[1] = v.y; rb[2] = v.z; rb[3] = v.w;
+      } else {
+        const float2 v = __ldg(reinterpret_cast<const float2 *>(B + kb * ldb + n));
+        rb[0] = v.x; rb[1] = v.y;
+      }
     } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) rb[c] = (kb < K && n + c < N) ? __ldg(B + kb * ldb + n + c) : 0.0f;
+      for (int c = 0; c < EB; ++c) rb[c] = (kb < K && n + c < N) ? __ldg(B + kb * ldb + n + c) : 0.0f;
     }
   };
   auto sstore = [&](int buf) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) As[buf][ak + c][ar] = ra[c];
-    *reinterpret_cast<float4 *>(&Bs[buf][bk][bc]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    for (int c = 0; c < EA; ++c) As[buf][ak + c][ar] = ra[c];
+#pragma unroll
+    for (int c = 0; c < EB; ++c) Bs[buf][bk][bc + c] = rb[c];
   };
   auto step = [&](int buf, int kk) {
-    const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][4 * ty]);
-    const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + 4 * ty]);
-    const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][4 * tx]);
-    const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][64 + 4 * tx]);
-    const float a[STM] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const float b[STN] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    float a[4 * HM], b[4 * HN];
 #pragma unroll
-    for (int i = 0; i < STM; ++i)
+    for (int h = 0; h < HM; ++h) {
+      const float4 v = *reinterpret_cast<const float4 *>(&As[buf][kk][64 * h + 4 * ty]);
+      a[4 * h] = v.x; a[4 * h + 1] = v.y; a[4 * h + 2] = v.z; a[4 * h + 3] = v.w;
+    }
 #pragma unroll
-      for (int j = 0; j < STN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    for (int g = 0; g < HN; ++g) {
+      const float4 v = *reinterpret_cast<const float4 *>(&Bs[buf][kk][64 * g + 4 * tx]);
+      b[4 * g] = v.x; b[4 * g + 1] = v.y; b[4 * g + 2] = v.z; b[4 * g + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 4 * HM; ++i)
+#pragma unroll
+      for (int j = 0; j < 4 * HN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
   };
 
   const int64_t ntiles = (K + SBK - 1) / SBK;
@@ -120,17 +137,17 @@ __global__ void __launch_bounds__(256, 2) gemm_simt_kernel(const float *__restri
   }
 
 #pragma unroll
-  for (int i = 0; i < STM; ++i) {
-    const int64_t m = m0 + (i < 4 ? 4 * ty + i : 64 + 4 * ty + (i - 4));
+  for (int i = 0; i < 4 * HM; ++i) {
+    const int64_t m = m0 + 64 * (i / 4) + 4 * ty + (i % 4);
     if (m >= M) continue;
 #pragma unroll
-    for (int jh = 0; jh < 2; ++jh) {
-      const int64_t n = n0 + 64 * jh + 4 * tx;
+    for (int g = 0; g < HN; ++g) {
+      const int64_t n = n0 + 64 * g + 4 * tx;
       float v[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int64_t nn = n + j;
-        v[j] = acc[i][4 * jh + j];
+        v[j] = acc[i][4 * g + j];
         if (nn < N) {
           if (EPI == EPI_MBR) v[j] = relu_max(__fadd_rn(v[j], aux[nn]));
           else if (EPI == EPI_ADD) v[j] = __fadd_rn(v[j], aux[m * ldc + nn]);
@@ -189,16 +206,25 @@ int grid_for(int64_t work, int threads) {
 
 }  // namespace
 
+// 128x128 tiles, or 64x64 when there are fewer 128x128 tiles than SMs (4x the CTAs).
+static int simt_tile(int64_t M, int64_t N) {
+  const int64_t tiles = ((M + 127) / 128) * ((N + 127) / 128);
+  return tiles < 148 ? 64 : 128;
+}
+
 void simt_launch_shape(int64_t M, int64_t N, int grid[3], int block[3], int *smem) {
-  grid[0] = (int)((N + SBN - 1) / SBN);
-  grid[1] = (int)((M + SBM - 1) / SBM);
+  const int t = simt_tile(M, N);
+  grid[0] = (int)((N + t - 1) / t);
+  grid[1] = (int)((M + t - 1) / t);
   grid[2] = 1;
   block[0] = 256;
   block[1] = block[2] = 1;
   *smem = 0;
 }
 
-// Float4 global access needs 16-byte-aligned bases and pitches (C_res shares ldc).
+int simt_tile_size(int64_t M, int64_t N) { return simt_tile(M, N); }
+
+// Vector global access needs 16-byte-aligned bases and pitches (C_res shares ldc).
 static bool simt_vec_ok(const float *A, const float *B, const float *aux, const float *C, int64_t lda, int64_t ldb,
                         int64_t ldc, int epi) {
   auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -206,30 +232,38 @@ static bool simt_vec_ok(const float *A, const float *B, const float *aux, const 
          (epi != EPI_ADD || al(aux));
 }
 
+template <int EPI, int T>
+static void launch_simt_tile(bool vec, cudaStream_t stream, const float *A, const float *B, const float *aux,
+                             float *C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc) {
+  const dim3 grid((unsigned)((N + T - 1) / T), (unsigned)((M + T - 1) / T));
+  if (vec) gemm_simt_kernel<EPI, true, T, T><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
+  else gemm_simt_kernel<EPI, false, T, T><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
+}
+
 template <int EPI>
-static void launch_simt_epi(bool vec, dim3 grid, cudaStream_t stream, const float *A, const float *B,
+static void launch_simt_epi(bool vec, int tile, cudaStream_t stream, const float *A, const float *B,
                             const float *aux, float *C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                             int64_t ldc) {
-  if (vec) gemm_simt_kernel<EPI, true><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
-  else gemm_simt_kernel<EPI, false><<<grid, 256, 0, stream>>>(A, B, aux, C, M, N, K, lda, ldb, ldc);
+  if (tile == 64) launch_simt_tile<EPI, 64>(vec, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
+  else launch_simt_tile<EPI, 128>(vec, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
 }
 
 cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const float *aux, float *C,
                              int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                              int64_t ldc, cudaStream_t stream) {
   if (M == 0 || N == 0) return cudaSuccess;
-  dim3 grid((unsigned)((N + SBN - 1) / SBN), (unsigned)((M + SBM - 1) / SBM));
   const bool vec = simt_vec_ok(A, B, aux, C, lda, ldb, ldc, epi);
-  if (epi == EPI_MATMUL) launch_simt_epi<EPI_MATMUL>(vec, grid, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
-  else if (epi == EPI_MBR) launch_simt_epi<EPI_MBR>(vec, grid, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
-  else launch_simt_epi<EPI_ADD>(vec, grid, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
+  const int tile = simt_tile(M, N);
+  if (epi == EPI_MATMUL) launch_simt_epi<EPI_MATMUL>(vec, tile, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
+  else if (epi == EPI_MBR) launch_simt_epi<EPI_MBR>(vec, tile, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
+  else launch_simt_epi<EPI_ADD>(vec, tile, stream, A, B, aux, C, M, N, K, lda, ldb, ldc);
   return cudaGetLastError();
 }
 
 cudaError_t simt_func_attributes(int epi, cudaFuncAttributes *a, int *blocks) {
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MBR, true>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_ADD, true>)
-                                   : reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MATMUL, true>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MBR, true, 128, 128>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_simt_kernel<EPI_ADD, true, 128, 128>)
+                                   : reinterpret_cast<const void *>(gemm_simt_kernel<EPI_MATMUL, true, 128, 128>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, f, 256, 0);

@@ -21,8 +21,9 @@ from tensorforge_b200 import _lib, tforge_cpu as tc, tforge_gpu as tg
 
 pytestmark = pytest.mark.gpu
 
+# 1664x1536x96 has 156 tiles of 128x128 (the large-tile SIMT kernel); the others use 64x64.
 EXACT_SHAPES = [(256, 256, 128), (777, 1111, 333), (1000, 1000, 1000), (7, 19, 5), (1, 1, 1),
-                (130, 260, 36), (256, 256, 0)]
+                (130, 260, 36), (256, 256, 0), (1664, 1536, 96), (1665, 1537, 97)]
 TC_SHAPES = [(256, 256, 128), (2048, 2048, 2048), (1000, 1000, 1000), (512, 512, 4096), (129, 264, 36),
              (300, 8, 64), (4, 2048, 128), (1, 4, 16), (513, 1000, 520), (128, 256, 2048)]
 
