@@ -174,7 +174,7 @@ double est_cost(int64_t M, int64_t N, int tile_m, int tile_n, int ctas_per_tile,
 }
 
 bool config_supported(const TcConfig &c) {
-  if (c.pair) return c.bn == 256 && pair_smem_bytes(c.prec, c.stages) > 0;
+  if (c.pair) return (c.bn == 256 || c.bn == 240) && pair_smem_bytes(c.prec, c.stages) > 0;
   return tc_config_supported(c);
 }
 
@@ -214,9 +214,23 @@ bool tuned_tc(int prec, int64_t M, int64_t N, int64_t K, TcConfig *out) {
   return true;
 }
 
+int device_pairs();
+int auto_pair_splits(int prec, int64_t M, int64_t N, int64_t K);
+
+// Tile width of the pair kernel without split-K: 240 instead of 256 columns when that takes
+// no more waves of SM pairs, so each wave's tiles are 1/16 narrower (2048 x 2048: 72 tiles
+// of 256 x 240 on 74 pairs instead of 64 tiles of 256 x 256, 86 % of the pairs busy).
+int pair_width(int prec, int64_t M, int64_t N, int64_t K) {
+  if (auto_pair_splits(prec, M, N, K) > 1) return 256;
+  const int64_t pairs = device_pairs(), tm = (M + 255) / 256;
+  const int64_t w256 = (tm * ((N + 255) / 256) + pairs - 1) / pairs;
+  const int64_t w240 = (tm * ((N + 239) / 240) + pairs - 1) / pairs;
+  return w240 * 240 < w256 * 256 ? 240 : 256;
+}
+
 // Analytic fallback outside the measured range: the fewest waves over the tile area.
-TcConfig model_tc(int prec, int64_t M, int64_t N) {
-  TcConfig best{prec, 256, kStagesPair[prec], 1};
+TcConfig model_tc(int prec, int64_t M, int64_t N, int64_t K) {
+  TcConfig best{prec, pair_width(prec, M, N, K), kStagesPair[prec], 1};
   double best_cost = est_cost(M, N, 256, 256, 2, kKernelEff[0]);
   const int bns[3] = {256, 128, 64};
   for (int i = 0; i < 3; ++i) {
@@ -232,7 +246,7 @@ TcConfig model_tc(int prec, int64_t M, int64_t N) {
 TcConfig table_tc(int prec, int64_t M, int64_t N, int64_t K) {
   TcConfig c{};
   if (tuned_tc(prec, M, N, K, &c)) return c;
-  return model_tc(prec, M, N);
+  return model_tc(prec, M, N, K);
 }
 
 Choice choose(int mode, int64_t M, int64_t N, int64_t K, bool tma_ok) {
@@ -249,10 +263,11 @@ Choice choose(int mode, int64_t M, int64_t N, int64_t K, bool tma_ok) {
     c.kind = K_SIMT;
   } else if (g_cfg.kernel == 1 || g_cfg.kernel == 3) {
     const int pair = g_cfg.kernel == 3;
-    TcConfig f{prec, pair ? 256 : (g_cfg.bn ? g_cfg.bn : (c.tc.pair ? 256 : c.tc.bn)), 0, pair};
+    TcConfig f{prec, pair ? (g_cfg.bn == 240 ? 240 : 256) : (g_cfg.bn ? g_cfg.bn : (c.tc.pair ? 256 : c.tc.bn)), 0,
+               pair};
     f.stages = g_cfg.stages ? g_cfg.stages
                             : (pair ? kStagesPair[prec] : kStages1[prec][f.bn == 256 ? 0 : (f.bn == 128 ? 1 : 2)]);
-    if (config_supported(f)) c.tc = f;
+    if (config_supported(f) && !(pair && f.bn == 240 && g_cfg.split_k > 1)) c.tc = f;
     else c.kind = -1;
   }
   return c;
@@ -323,7 +338,11 @@ int pair_splits(const TcConfig &c, int64_t M, int64_t N, int64_t K) {
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     if (g_cfg.kernel == 3 && g_cfg.split_k > 0) return g_cfg.split_k;
   }
-  if (c.prec == PREC_BF16) return 1;
+  return c.bn == 256 ? auto_pair_splits(c.prec, M, N, K) : 1;
+}
+
+int auto_pair_splits(int prec, int64_t M, int64_t N, int64_t K) {
+  if (prec == PREC_BF16) return 1;
   const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
   const int64_t kb = (K + 31) / 32;
   const int64_t pairs = device_pairs();
@@ -377,7 +396,7 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
     }
     p.splits = splits;
     p.split_rows = (int32_t)mp;
-    e = launch_gemm_pair(cfg.prec, cfg.stages, EPI_MATMUL, tmA, tmB, tmW, tmW, p, st);
+    e = launch_gemm_pair(cfg.prec, cfg.stages, cfg.bn, EPI_MATMUL, tmA, tmB, tmW, tmW, p, st);
     if (e == cudaSuccess)
       e = launch_splitk_reduce(epi, static_cast<const float *>(ws), splits, mp * a->N, a->M, a->N, a->bias, a->C_res,
                                a->out, ldc, st);
@@ -391,7 +410,7 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
       rc = make_tmap(&tmC, a->C_res, false, a->M, a->N, ldc, 32, 128);
       if (rc) return rc;
     }
-    e = launch_gemm_pair(cfg.prec, cfg.stages, epi, tmA, tmB, tmO, tmC, p, st);
+    e = launch_gemm_pair(cfg.prec, cfg.stages, cfg.bn, epi, tmA, tmB, tmO, tmC, p, st);
   } else {
     e = launch_gemm_tc(cfg, epi, tmA, tmB, p, st);
   }
@@ -624,7 +643,7 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
   if (have_dev) {
     cudaFuncAttributes fa{};
     int blocks = 0;
-    cudaError_t e = c.tc.pair ? pair_func_attributes(c.tc.prec, c.tc.stages, epi, &fa, &blocks)
+    cudaError_t e = c.tc.pair ? pair_func_attributes(c.tc.prec, c.tc.stages, c.tc.bn, epi, &fa, &blocks)
                               : tc_func_attributes(c.tc, epi, &fa, &blocks);
     fill_attrs(e, fa, blocks);
   }

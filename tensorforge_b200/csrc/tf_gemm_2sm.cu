@@ -9,29 +9,34 @@
 // fp32-accurate mode (3xTF32): per K step the MMA issues lo*hi, hi*lo and hi*hi.  The
 // split of A goes to tensor memory (tcgen05.st), so the MMAs read only B from shared
 // memory.  Two rings: TMA lands raw A and B in a landing ring (kLand slots); converters
-// load a slot, free it at once, and write the split operands into an operand ring (kOps
-// slots: B hi and lo in shared memory, A hi and lo in TMEM), which the MMAs free.  So the
-// TMA round trip does not include the MMAs, and the MMA round trip does not include TMA.
+// load a slot and write the split operands into an operand ring (kOps slots: B lo in
+// shared memory, A hi and lo in TMEM), which the MMAs free.  B hi is the raw B of the
+// landing slot (truncation split), which the MMAs read in place, so a landing slot is
+// free once its converters have loaded it and the MMAs reading its B are done.
 // 384 threads per CTA:
 //
 //   warp 0       TMA producer (each CTA): A tile and B half of k-block kb -> landing slot
-//                kb % kLand (full[l]) once this CTA's converters freed it (lempty[l]).
+//                l = kb % kLand (full[l]) once slot l is free (lempty[l]).
 //   warps 2..11  converters (each CTA): load the landing slot, arrive lempty[l], wait
-//                until operand slot o = kb % kOps is free (empty[o]), write B hi and lo
-//                there; warps 4..11 also split A: warp w takes rows 32 (w % 4) .. +31 (its
-//                TMEM lane quadrant) and K half (w - 4) / 4, into TMEM columns
-//                [256 + 64 o, +32) (hi) and [+32, +32) (lo).  Then each warp arrives on
-//                this CTA's conv[o].
-//   warp 1       leader CTA: issues the pair MMAs into TMEM columns [0, 256) of both CTAs
-//                once its conv[o] and ready[o] (the peer's) completed; a multicast
-//                tcgen05.commit frees operand slot o in both CTAs (empty[o]), a last one
-//                signals accf in both.  Peer CTA: relays its conv[o] to the leader's
-//                ready[o] with one st.async token per k-block.
-//   warps 4..11  epilogue (each CTA): its 128 rows x 256 columns from its own TMEM.
+//                until operand slot o = kb % kOps is free (empty[o]), write B lo there;
+//                warps 4..11 also split A: warp w takes rows 32 (w % 4) .. +31 (its TMEM
+//                lane quadrant) and K half (w - 4) / 4, into TMEM columns [256 + 64 o, +32)
+//                (hi) and [+32, +32) (lo).  Then each warp arrives on this CTA's conv[o].
+//   warp 1       leader CTA: issues the pair MMAs into TMEM columns [0, BN) of both CTAs
+//                once its conv[o] and ready[o] (the peer's) completed; multicast
+//                tcgen05.commits free operand slot o (empty[o]) and landing slot l
+//                (lempty[l]) in both CTAs, a last one signals accf in both.  Peer CTA:
+//                relays its conv[o] to the leader's ready[o] with one st.async token per
+//                k-block.
+//   warps 4..11  epilogue (each CTA): its 128 rows x BN columns from its own TMEM.
 //
 // The split (kPairSplit): the tensor core reads an f32 operand as TF32 by dropping its low
 // 13 mantissa bits, so the truncation split keeps hi = x and computes only
-// lo = x - trunc(x), exact in f32.  The round split (cvt.rna) is kept as an alternative.
+// lo = x - trunc(x), exact in f32.  The round split (cvt.rna) is kept as an alternative;
+// it writes B hi into the operand slot as well.
+//
+// Tile width BN: 256, or 240 when that needs no more waves of SM pairs (each CTA's MMA
+// half is then the first 120 of the 128 B columns it loads).
 //
 // TF32 / BF16 modes have no converters: each CTA's TMA (.cta_group::2 form) completes on
 // the LEADER's full[s], which expects both CTAs' bytes, and the MMA reads A and B from
@@ -47,12 +52,6 @@
 
 namespace tf {
 
-#ifndef TF_PAIR_SPLIT
-#define TF_PAIR_SPLIT 1
-#endif
-// 3xTF32 operand split of the pair kernel: 1 = truncation split, 0 = round split.
-constexpr int kPairSplit = TF_PAIR_SPLIT;
-
 #ifndef TF_RASTER_GROUP
 #define TF_RASTER_GROUP 8
 #endif
@@ -64,8 +63,11 @@ namespace {
 #ifndef TF_PAIR_OPS
 #define TF_PAIR_OPS 3
 #endif
-// 3xTF32: depth of the operand ring (B hi/lo in shared memory, A hi/lo in TMEM).
+// 3xTF32: depth of the operand ring (B lo in shared memory, A hi/lo in TMEM).
 constexpr int kPairOps = TF_PAIR_OPS;
+// Truncation split: B hi is the raw f32 B as TMA landed it (the tensor core drops the low
+// 13 bits itself), so the MMAs read it from the landing slot and only B lo is written.
+constexpr bool kPairHiDirect = kPairSplit == 1;
 
 template <int PREC, int STAGES>
 struct PairLayout {
@@ -86,14 +88,15 @@ struct PairLayout {
   static constexpr int kBBytes = kBNHalf * kBK * kElem;
   static constexpr int kStageBytes = kABytes + kBBytes;
   // Landing ring (TMA destination): kLand slots of A + B.  TF32/BF16: the MMA reads them
-  // in place.  3xTF32: the converters empty a slot as soon as they have loaded it, into the
-  // operand ring of kOps slots -- B hi and B lo in shared memory, A hi and lo in TMEM --
-  // which the MMAs empty.  TMA latency then overlaps the MMAs of the operand ring.
+  // in place.  3xTF32: the converters load a slot into the operand ring of kOps slots --
+  // B lo in shared memory, A hi and lo in TMEM -- which the MMAs empty; the MMAs read
+  // B hi from the landing slot itself.
   static constexpr int kLand = STAGES;
   static constexpr int kOps = kX3 ? kPairOps : STAGES;
-  static constexpr int kOpBytes = kX3 ? 2 * kBBytes : 0;
+  // Operand slot: B lo (and B hi unless the MMAs read it from the landing slot).
+  static constexpr int kOpBytes = kX3 ? (kPairHiDirect ? kBBytes : 2 * kBBytes) : 0;
   static constexpr int kRingBytes = kLand * kStageBytes + kOps * kOpBytes;
-  // Barriers: full[kLand], lempty[kLand] (3xTF32: converters -> producer), conv[kOps],
+  // Barriers: full[kLand], lempty[kLand] (3xTF32: converters + MMAs -> producer), conv[kOps],
   // ready[kOps], empty[kOps] (MMA commit), accf, resf.
   static constexpr int kNumBars = 2 * kLand + 3 * kOps + 3;
   // barriers, then tmem slot, abort flag, epilogue flag, spare, and one mailbox word per
@@ -108,8 +111,8 @@ struct PairLayout {
   static constexpr int kConvWarps = 10;                // warps 2..11 (3xTF32)
   __host__ __device__ static constexpr int a_off(int l) { return l * kStageBytes; }
   __host__ __device__ static constexpr int b_off(int l) { return l * kStageBytes + kABytes; }
-  __host__ __device__ static constexpr int hi_off(int o) { return kLand * kStageBytes + o * kOpBytes; }
-  __host__ __device__ static constexpr int lo_off(int o) { return hi_off(o) + kBBytes; }
+  __host__ __device__ static constexpr int lo_off(int o) { return kLand * kStageBytes + o * kOpBytes; }
+  __host__ __device__ static constexpr int hi_off(int o) { return lo_off(o) + kBBytes; }  // copy only
   __host__ __device__ static constexpr int bar_off() { return kRingBytes; }
   __host__ __device__ static constexpr uint32_t a_tmem_col(int o) { return kAccCols + 64u * o; }
   static_assert(!kX3 || kAccCols + 64u * kOps <= 512u, "TMEM budget");
@@ -165,7 +168,7 @@ __device__ __forceinline__ void relay_stages(uint32_t conv0, uint32_t ready0, ui
   }
 }
 
-template <int PREC, int STAGES, int EPI, int SPLIT>
+template <int PREC, int STAGES, int EPI, int SPLIT, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STAGES>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmC,
@@ -173,7 +176,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   using L = PairLayout<PREC, STAGES>;
   constexpr bool kX3 = PREC == PREC_X3;
   constexpr bool kTF32 = PREC != PREC_BF16;
-  constexpr uint32_t kIdesc = instr_desc(kTF32 ? 2u : 1u, 256, 256);
+  constexpr uint32_t kIdesc = instr_desc(kTF32 ? 2u : 1u, 256, BN);
+  // BN = 240: each CTA's MMA half is 120 B columns (the first 120 of the 128 it loads), and
+  // the accumulator's last 32-column chunk holds only 16 output columns.
+  static_assert(BN == 256 || BN == 240, "pair tile width");
+  constexpr int kHalfN = BN / 2;
+  constexpr bool kHalfChunk = BN % 32 != 0;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -206,7 +214,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   const int group_m = tiles_m - first_m < kRasterGroup ? tiles_m - first_m : kRasterGroup;
   const int tile_m = first_m + (pid - group * per_group) % group_m;
   const int tile_n = (pid - group * per_group) / group_m;
-  const int n0 = tile_n * 256, m0 = tile_m * 256 + (int)rank * 128;
+  const int n0 = tile_n * BN, m0 = tile_m * 256 + (int)rank * 128;
   // Split-K: this pair takes k-blocks [kb0, kb0 + nkb) of the tile's K and stores raw
   // partial sums at row offset blockIdx.z * split_rows of the output map.
   const int nkb_all = (p.K + L::kBK - 1) / L::kBK;
@@ -219,7 +227,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   if (threadIdx.x == 0) {
     for (int l = 0; l < kL; ++l) {
       mbar_init(full0 + 8 * l, 1);
-      mbar_init(lempty0 + 8 * l, L::kConvWarps);
+      // 3xTF32 with B hi read in place: the pair MMAs' commit also frees the slot.
+      mbar_init(lempty0 + 8 * l, L::kConvWarps + (kPairHiDirect ? 1 : 0));
     }
     for (int o = 0; o < kO; ++o) {
       mbar_init(conv0 + 8 * o, L::kConvWarps);
@@ -275,7 +284,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       }
       if (p.debug_skip && kb == 0) continue;  // test hook: this stage never fills
       const int kc = (kb0 + kb) * L::kBK;
-      const int nb = n0 + (int)rank * L::kBNHalf;
+      const int nb = n0 + (int)rank * kHalfN;
       if constexpr (kX3) {
         mbar_arrive_expect_tx(full0 + 8 * s, L::kStageBytes);
         tma_load_2d(sbase + L::a_off(s), &tmA, kc, m0, full0 + 8 * s);
@@ -318,14 +327,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
           if (!mbar_wait_cluster(full0 + 8 * s, round & 1, wc)) break;
         }
         tc_fence_after();
+        const int land = kb % kL;  // 3xTF32: landing slot holding this k-block's raw B (= B hi)
 #pragma unroll
         for (int ks = 0; ks < L::kKSteps; ++ks) {
           if constexpr (kX3) {
             const uint32_t a_hi = tmem + L::a_tmem_col(s) + 8 * ks, a_lo = a_hi + 32;
             const uint64_t bl = smem_desc(sbase + L::lo_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
                                           L::kBSbo, L::kBSwz);
-            const uint64_t bh = smem_desc(sbase + L::hi_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
-                                          L::kBSbo, L::kBSwz);
+            const uint64_t bh = smem_desc(sbase + (kPairHiDirect ? L::b_off(land) : L::hi_off(s)) +
+                                              ks * L::kUmmaK * 128,
+                                          L::kBK * 128, L::kBSbo, L::kBSwz);
             mma_ts_pair_tf32(tmem, a_lo, bh, kIdesc, accum);
             mma_ts_pair_tf32(tmem, a_hi, bl, kIdesc, 1u);
             mma_ts_pair_tf32(tmem, a_hi, bh, kIdesc, 1u);
@@ -338,6 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
           accum = 1u;
         }
         mma_commit_pair(empty0 + 8 * s, 0x3);
+        if constexpr (kX3 && kPairHiDirect) mma_commit_pair(lempty0 + 8 * land, 0x3);
       }
       mma_commit_pair(accf, 0x3);
       if (*abort_flag) mbar_wait_drain_cluster(accf, 0, p.limit_ns);
@@ -348,10 +360,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
     // ---------------- 3xTF32 converters (both CTAs, warps 2..11) ----------------
     // k-block kb: landing slot l = kb % kLand, operand slot o = kb % kOps.  Each thread
     // loads its B chunks (t + 320 i) and, in warps 4..11, four 16-B chunks of A row r (K
-    // half h), and releases the landing slot (lempty[l]) before it splits.  It then waits
-    // until the MMAs of k-block kb - kOps have finished with operand slot o (empty[o]) and
-    // writes B hi and lo there at the offsets TMA used (same swizzle), and A hi and lo into
-    // the TMEM columns of slot o.
+    // half h), and arrives on lempty[l] before it splits.  It then waits until the MMAs of
+    // k-block kb - kOps have finished with operand slot o (empty[o]) and writes B lo there
+    // at the offsets TMA used (same swizzle), and A hi and lo into the TMEM columns of
+    // slot o.
     const int t = threadIdx.x - 64;
     constexpr int kChunks = L::kBBytes / 16;
     const int q = warp & 3, h = (warp - 4) >> 2, r = q * 32 + lane;
@@ -379,10 +391,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       for (int i = 0; i < 4; ++i) {
         const int c = t + 320 * i;
         if (c < kChunks) {
-          float4 hh, ll;
-          split4<SPLIT>(xb[i], hh, ll);
-          bhi[c] = hh;
-          blo[c] = ll;
+          if constexpr (kPairHiDirect) {
+            // B hi stays in the landing slot; a non-finite chunk (rare) gets its hi patched
+            // there (NaN kept quiet after the tensor core drops the low 13 bits).
+            bool special;
+            float4 ll = split_lo_trunc4(xb[i], special);
+            if (special) {
+              float4 hh;
+              split4<SPLIT>(xb[i], hh, ll);
+              reinterpret_cast<float4 *>(smem + L::b_off(l))[c] = hh;
+            }
+            blo[c] = ll;
+          } else {
+            float4 hh, ll;
+            split4<SPLIT>(xb[i], hh, ll);
+            bhi[c] = hh;
+            blo[c] = ll;
+          }
         }
       }
       fence_proxy_async_smem();
@@ -453,27 +478,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         tmem_ld_wait();
         const int col0 = n0 + c * 32;
         uint8_t *box = smem + c * L::kEpiBoxBytes + r * 128;
+        // Epilogue of columns col0 + 4 j .. + 3 (matmul_add: the residual sits in the box).
+        auto finish = [&](int j) {
+          float4 v = make_float4(__uint_as_float(rr[4 * j]), __uint_as_float(rr[4 * j + 1]),
+                                 __uint_as_float(rr[4 * j + 2]), __uint_as_float(rr[4 * j + 3]));
+          if constexpr (EPI == EPI_MBR) {
+            const float4 b = bias_s[c * 8 + j];
+            v.x = relu_ieee(__fadd_rn(v.x, b.x));
+            v.y = relu_ieee(__fadd_rn(v.y, b.y));
+            v.z = relu_ieee(__fadd_rn(v.z, b.z));
+            v.w = relu_ieee(__fadd_rn(v.w, b.w));
+          } else if constexpr (EPI == EPI_ADD) {
+            const float4 cr = *reinterpret_cast<const float4 *>(box + ((j ^ (r & 7)) << 4));
+            v.x = __fadd_rn(v.x, cr.x);
+            v.y = __fadd_rn(v.y, cr.y);
+            v.z = __fadd_rn(v.z, cr.z);
+            v.w = __fadd_rn(v.w, cr.w);
+          }
+          return v;
+        };
+        if (kHalfChunk && c == 7) {
+          // The last 16 columns of a 240-wide tile: the other half of a 32-column box
+          // belongs to the next tile, so each thread stores its row's 16 values directly
+          // (no split-K on this width: out_row0 == m0).
+          if (res_ok && m0 + r < p.M && col0 < p.N) {
+            float *orow = p.out + (int64_t)(m0 + r) * p.ldc;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 v = finish(j);
+              const int col = col0 + 4 * j;
+              if (col + 3 < p.N) {
+                *reinterpret_cast<float4 *>(orow + col) = v;
+              } else {
+                if (col < p.N) orow[col] = v.x;
+                if (col + 1 < p.N) orow[col + 1] = v.y;
+                if (col + 2 < p.N) orow[col + 2] = v.z;
+              }
+            }
+          }
+          continue;  // every warp of this chunk takes this branch: no named barrier
+        }
         if (res_ok && cta_rows && col0 < p.N) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 v = make_float4(__uint_as_float(rr[4 * j]), __uint_as_float(rr[4 * j + 1]),
-                                   __uint_as_float(rr[4 * j + 2]), __uint_as_float(rr[4 * j + 3]));
-            float4 *slot = reinterpret_cast<float4 *>(box + ((j ^ (r & 7)) << 4));
-            if constexpr (EPI == EPI_MBR) {
-              const float4 b = bias_s[c * 8 + j];  // bias of columns col0 + 4 j .. + 3
-              v.x = relu_ieee(__fadd_rn(v.x, b.x));
-              v.y = relu_ieee(__fadd_rn(v.y, b.y));
-              v.z = relu_ieee(__fadd_rn(v.z, b.z));
-              v.w = relu_ieee(__fadd_rn(v.w, b.w));
-            } else if constexpr (EPI == EPI_ADD) {
-              const float4 cr = *slot;
-              v.x = __fadd_rn(v.x, cr.x);
-              v.y = __fadd_rn(v.y, cr.y);
-              v.z = __fadd_rn(v.z, cr.z);
-              v.w = __fadd_rn(v.w, cr.w);
-            }
-            *slot = v;
-          }
+          for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(box + ((j ^ (r & 7)) << 4)) = finish(j);
         }
         fence_proxy_async_smem();
         named_barrier(1 + c, 128);
@@ -495,11 +542,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   }
 }
 
-template <int PREC, int STAGES, int EPI>
+template <int PREC, int STAGES, int EPI, int BN>
 cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
                             const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   using L = PairLayout<PREC, STAGES>;
-  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit>;
+  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit, BN>;
+  // The 240-wide tile stores its last 16 columns through p.out, so it takes no split-K.
+  if (BN != 256 && p.splits > 1) return cudaErrorInvalidValue;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -509,28 +558,28 @@ cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, cons
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
-  dim3 grid(2 * ((p.N + 255) / 256), (p.M + 255) / 256, p.splits > 1 ? p.splits : 1);
+  dim3 grid(2 * ((p.N + BN - 1) / BN), (p.M + 255) / 256, p.splits > 1 ? p.splits : 1);
   kern<<<grid, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, tmO, tmC, p);
   return cudaGetLastError();
 }
 
-template <int PREC, int STAGES>
+template <int PREC, int STAGES, int BN>
 cudaError_t launch_pair_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
                             const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   switch (epi) {
-    case EPI_MATMUL: return launch_pair_one<PREC, STAGES, EPI_MATMUL>(tmA, tmB, tmO, tmC, p, stream);
-    case EPI_MBR: return launch_pair_one<PREC, STAGES, EPI_MBR>(tmA, tmB, tmO, tmC, p, stream);
-    case EPI_ADD: return launch_pair_one<PREC, STAGES, EPI_ADD>(tmA, tmB, tmO, tmC, p, stream);
+    case EPI_MATMUL: return launch_pair_one<PREC, STAGES, EPI_MATMUL, BN>(tmA, tmB, tmO, tmC, p, stream);
+    case EPI_MBR: return launch_pair_one<PREC, STAGES, EPI_MBR, BN>(tmA, tmB, tmO, tmC, p, stream);
+    case EPI_ADD: return launch_pair_one<PREC, STAGES, EPI_ADD, BN>(tmA, tmB, tmO, tmC, p, stream);
   }
   return cudaErrorInvalidValue;
 }
 
-template <int PREC, int STAGES>
+template <int PREC, int STAGES, int BN>
 cudaError_t pair_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
   using L = PairLayout<PREC, STAGES>;
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit>)
-                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit, BN>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit, BN>)
+                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit, BN>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
@@ -553,19 +602,21 @@ int pair_smem_bytes(int prec, int stages) {
 
 int pair_tmem_cols(int prec) { return prec == PREC_X3 ? 512 : 256; }
 
-cudaError_t launch_gemm_pair(int prec, int stages, int epi, const CUtensorMap &tmA,
+cudaError_t launch_gemm_pair(int prec, int stages, int bn, int epi, const CUtensorMap &tmA,
                              const CUtensorMap &tmB, const CUtensorMap &tmO, const CUtensorMap &tmC,
                              const TcParams &p, cudaStream_t stream) {
-#define TF_PLAUNCH(P, S) \
-  if (prec == P && stages == S) return launch_pair_epi<P, S>(epi, tmA, tmB, tmO, tmC, p, stream);
+#define TF_PLAUNCH(P, S)                                                                              \
+  if (prec == P && stages == S && bn == 256) return launch_pair_epi<P, S, 256>(epi, tmA, tmB, tmO, tmC, p, stream); \
+  if (prec == P && stages == S && bn == 240) return launch_pair_epi<P, S, 240>(epi, tmA, tmB, tmO, tmC, p, stream);
   TF_PAIR_CONFIGS(TF_PLAUNCH)
 #undef TF_PLAUNCH
   return cudaErrorInvalidValue;
 }
 
-cudaError_t pair_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *a, int *blocks) {
-#define TF_PATTR(P, S) \
-  if (prec == P && stages == S) return pair_attrs<P, S>(epi, a, blocks);
+cudaError_t pair_func_attributes(int prec, int stages, int bn, int epi, cudaFuncAttributes *a, int *blocks) {
+#define TF_PATTR(P, S)                                                               \
+  if (prec == P && stages == S && bn == 256) return pair_attrs<P, S, 256>(epi, a, blocks); \
+  if (prec == P && stages == S && bn == 240) return pair_attrs<P, S, 240>(epi, a, blocks);
   TF_PAIR_CONFIGS(TF_PATTR)
 #undef TF_PATTR
   return cudaErrorInvalidValue;

@@ -13,8 +13,14 @@ enum Epi : int { EPI_MATMUL = 0, EPI_MBR = 1, EPI_ADD = 2 };
 // Tensor-core precision paths: one TF32 product, the 3xTF32 split, or bf16 operands.
 enum Prec : int { PREC_TF32 = 0, PREC_X3 = 1, PREC_BF16 = 2 };
 
+#ifndef TF_PAIR_SPLIT
+#define TF_PAIR_SPLIT 1
+#endif
+// 3xTF32 operand split of the pair kernel: 1 = truncation split, 0 = round split.
+constexpr int kPairSplit = TF_PAIR_SPLIT;
+
 #ifndef TF_PAIR_X3_LAND
-#define TF_PAIR_X3_LAND 4
+#define TF_PAIR_X3_LAND (TF_PAIR_SPLIT ? 5 : 4)
 #endif
 // Landing-ring depth of the 3xTF32 pair kernel (its instantiated "stages").
 constexpr int kPairX3Land = TF_PAIR_X3_LAND;
@@ -57,15 +63,17 @@ cudaError_t tc_func_attributes(const TcConfig &cfg, int epi, cudaFuncAttributes 
                                int *blocks_per_sm);
 cudaError_t simt_func_attributes(int epi, cudaFuncAttributes *attr, int *blocks_per_sm);
 
-// CTA-pair (cta_group::2) kernel: 256 x 256 output tiles, clusters of two CTAs.
+// CTA-pair (cta_group::2) kernel: 256-row x bn-column output tiles (bn 256 or 240),
+// clusters of two CTAs.
 int pair_smem_bytes(int prec, int stages);
 int pair_tmem_cols(int prec);
 // tmO / tmC: f32 maps of the output and of C_res (box 32 columns x 128 rows, 128-B
-// swizzle) for the TMA-store epilogue; tmC is read only by matmul_add.
-cudaError_t launch_gemm_pair(int prec, int stages, int epi, const CUtensorMap &tmA,
+// swizzle) for the TMA-store epilogue; tmC is read only by matmul_add.  bn 240 takes no
+// split-K (p.splits <= 1).
+cudaError_t launch_gemm_pair(int prec, int stages, int bn, int epi, const CUtensorMap &tmA,
                              const CUtensorMap &tmB, const CUtensorMap &tmO, const CUtensorMap &tmC,
                              const TcParams &p, cudaStream_t stream);
-cudaError_t pair_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *attr,
+cudaError_t pair_func_attributes(int prec, int stages, int bn, int epi, cudaFuncAttributes *attr,
                                  int *blocks_per_sm);
 
 // The dispatch table's tensor-core choice (false when it would not use tcgen05), the

@@ -20,7 +20,7 @@ namespace tf {
 
 namespace {
 
-constexpr int SBM = 128, SBN = 128, SBK = 8, STM = 8, STN = 8;
+constexpr int SBK = 8;  // K per shared-memory stage
 
 // IEEE-2019 maximum(x, +0.0) with the NaN payload kept, on the bit pattern (a float
 // compare-and-select may be contracted into a max that canonicalizes NaN).

@@ -130,8 +130,9 @@ def test_tuned_table_entries_are_what_dispatch_picks():
         assert tflops > 0
         d = _lib.describe("mbr", m, n, k, modes[prec])
         assert d["kernel"].endswith("_pair") == bool(pair), (prec, m, n, k)
+        assert d["tile"][1] == bn, (prec, m, n, k)
         if not pair:  # the pair kernel has one instantiated depth per precision
-            assert d["stages"] == stages and d["tile"][1] == bn
+            assert d["stages"] == stages
     # (1100, 1000, 904) is nearest to the measured (1000, 1000, 1000) bf16 entry.
     assert _lib.describe("mbr", 1100, 1000, 904, "bf16")["tile"][1] == 64
 
@@ -147,9 +148,23 @@ def test_forced_config_and_reset():
         _lib.set_config(1, 96, 6)  # not instantiated
         with pytest.raises(_lib.TforgeError):
             _lib.describe("mbr", 2048, 2048, 2048, "tf32")
+        _lib.set_config(3, 240)  # 256 x 240 pair tiles
+        d = _lib.describe("mbr", 2048, 2048, 2048, "fp32")
+        assert d["tile"][:2] == [256, 240] and d["grid"][:2] == [18, 8] and d["split_k"] == 1
+        _lib.set_config(3, 240, split_k=2)  # the 240-wide tile takes no split-K
+        with pytest.raises(_lib.TforgeError):
+            _lib.describe("mbr", 2048, 2048, 2048, "fp32")
     finally:
         _lib.set_config()
     assert _lib.describe("mbr", 2048, 2048, 2048, "tf32")["kernel"] == "tf_gemm_tcgen05_tf32_pair"
+
+
+def test_model_picks_240_wide_pair_tiles_when_waves_allow():
+    """Outside the measured table the pair kernel takes 256 x 240 tiles when that needs no
+    more waves of SM pairs: 2048 x 2048 is 72 such tiles on 74 pairs instead of 64 of 256 x 256;
+    8192 x 8192 would need more waves and keeps 256."""
+    assert _lib.describe("mbr", 2048, 2048, 64, "fp32")["tile"][:2] == [256, 240]
+    assert _lib.describe("mbr", 65536, 65536, 64, "fp32")["tile"][:2] == [256, 256]
 
 
 def test_compile_kernel_writes_launch_json(tmp_path, monkeypatch):

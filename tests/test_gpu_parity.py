@@ -214,6 +214,45 @@ def test_pair_split_k_within_bound_and_deterministic(gpu, workload, mode, splits
     assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
 
 
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
+@pytest.mark.parametrize("workload", ["mbr", "matmul", "matmul_add"])
+@pytest.mark.parametrize("shape", [(300, 2152, 200), (520, 1936, 96), (256, 240, 64)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_pair_240_wide_tiles_within_bound(gpu, workload, mode, shape):
+    """256 x 240 pair tiles: each CTA's MMA half is the first 120 of the 128 B columns it
+    loads and the last 16 columns of a tile are stored without TMA.  N = 2152 ends inside a
+    tile's last 16 columns, N = 1936 leaves the last tile's second CTA wholly out of range,
+    256 x 240 is one tile; ragged M."""
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 23)
+    _lib.set_config(3, 240)
+    try:
+        d = _lib.describe(workload, m, n, k, mode)
+        assert d["tile"][1] == 240 and d["grid"][0] == 2 * -(-n // 240)
+        out = tg.run_op(workload, ins, m, n, k, mode)
+    finally:
+        _lib.set_config()
+    res = tc.check_output(workload, ins, out, mode)
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+
+
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
+def test_pair_240_matches_256_bitwise(gpu, mode):
+    """Each output element sees the same k-block order and the same per-k-step MMA sequence
+    whichever tile width covers it, so 256 x 240 and 256 x 256 tiles agree bit for bit (both
+    without split-K, which the 256-wide tiles would take here by default)."""
+    m, n, k = 512, 1024, 512
+    ins = tc.make_inputs("mbr", m, n, k, 29)
+    outs = []
+    for bn in (256, 240):
+        _lib.set_config(3, bn, split_k=1)
+        try:
+            outs.append(tg.run_op("mbr", ins, m, n, k, mode))
+        finally:
+            _lib.set_config()
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+
+
 def test_automatic_split_k_small_square(gpu):
     """1024^3 has 16 pair tiles for 74 SM pairs: the dispatch splits K and stays in bound."""
     d = _lib.describe("mbr", 1024, 1024, 1024, "fp32")
