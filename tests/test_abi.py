@@ -208,3 +208,14 @@ def test_csv_schema_is_the_references(tmp_path):
     w.close()
     rows = list(csv.DictReader(open(tmp_path / "r.csv")))
     assert rows[0]["workload"] == "mbr" and list(rows[0]) == provenance.FIELDS
+
+
+def test_autotune_table_round_trip(tmp_path):
+    """The sweep's table writer and reader agree (the reader backs `--merge`, which keeps the
+    entries of modes not swept)."""
+    from tensorforge_b200 import autotune
+    entries = autotune.read_table(autotune.TABLE)
+    assert len(entries) == len(_tune_table())
+    out = tmp_path / "t.inc"
+    autotune.write_table(entries, out)
+    assert autotune.read_table(out) == entries
