@@ -159,9 +159,10 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
 /* Force a kernel configuration (offline tuning sweeps); NULL restores the table. */
 typedef struct tforge_config {
   int32_t kernel;        /* 0 = table, 1 = tcgen05 one CTA per tile, 2 = SIMT, 3 = tcgen05 CTA pair */
-  int32_t bn;            /* 64, 128 or 256 (one-CTA kernel) */
+  int32_t bn;            /* 64, 128 or 256 (one-CTA kernel); 256 or 240 (CTA pair) */
   int32_t stages;
-  int32_t persistent;    /* reserved, 0 */
+  int32_t persistent;    /* 1 with kernel = 3: persistent CTA-pair kernel (TF32 / BF16 modes,
+                            256x256 tiles, two TMEM accumulators, no split-K) */
   int32_t split_k;       /* CTA-pair kernel in fp32 / TF32 mode: 0 = automatic, 1 = no split,
                             S = 2..8 pairs per tile, each over K / S */
 } tforge_config;

@@ -23,7 +23,8 @@ BUILD = PKG / "_build"
 LIB = PKG / "libtforge_gpu.so"
 RUNNER = PKG / "tforge-gpu-bench"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-LIB_SOURCES = ["tf_api.cu", "tf_gemm_tc.cu", "tf_gemm_2sm.cu", "tf_simt.cu", "tf_noalloc.cu", "tf_host.cu"]
+LIB_SOURCES = ["tf_api.cu", "tf_gemm_tc.cu", "tf_gemm_2sm.cu", "tf_simt.cu", "tf_noalloc.cu", "tf_host.cu",
+               "tf_gemm_2sm_persist.cu"]
 
 
 def nvcc() -> str:

@@ -174,12 +174,14 @@ double est_cost(int64_t M, int64_t N, int tile_m, int tile_n, int ctas_per_tile,
 }
 
 bool config_supported(const TcConfig &c) {
+  if (c.persist) return c.pair && c.bn == 256 && c.prec != PREC_X3 && persist_smem_bytes(c.prec, c.stages) > 0;
   if (c.pair) return (c.bn == 256 || c.bn == 240) && pair_smem_bytes(c.prec, c.stages) > 0;
   return tc_config_supported(c);
 }
 
 // Measured choices of the offline sweep (python -m tensorforge_b200.autotune on a B200):
 // the fastest instantiated configuration that passed the FP64 check, per (prec, M, N, K).
+// pair: 0 one-CTA kernel, 1 CTA-pair kernel, 2 persistent CTA-pair kernel.
 struct TuneEntry {
   int prec;
   int64_t m, n, k;
@@ -208,7 +210,7 @@ bool tuned_tc(int prec, int64_t M, int64_t N, int64_t K, TcConfig *out) {
   }
   if (!hit) return false;
   // The pair kernel has one instantiated depth per precision; the table says pair or not.
-  const TcConfig c{prec, hit->bn, hit->pair ? kStagesPair[prec] : hit->stages, hit->pair};
+  const TcConfig c{prec, hit->bn, hit->pair ? kStagesPair[prec] : hit->stages, hit->pair ? 1 : 0, hit->pair == 2};
   if (!config_supported(c)) return false;
   *out = c;
   return true;
@@ -264,10 +266,10 @@ Choice choose(int mode, int64_t M, int64_t N, int64_t K, bool tma_ok) {
   } else if (g_cfg.kernel == 1 || g_cfg.kernel == 3) {
     const int pair = g_cfg.kernel == 3;
     TcConfig f{prec, pair ? (g_cfg.bn == 240 ? 240 : 256) : (g_cfg.bn ? g_cfg.bn : (c.tc.pair ? 256 : c.tc.bn)), 0,
-               pair};
+               pair, pair && g_cfg.persistent ? 1 : 0};
     f.stages = g_cfg.stages ? g_cfg.stages
                             : (pair ? kStagesPair[prec] : kStages1[prec][f.bn == 256 ? 0 : (f.bn == 128 ? 1 : 2)]);
-    if (config_supported(f) && !(pair && f.bn == 240 && g_cfg.split_k > 1)) c.tc = f;
+    if (config_supported(f) && !(pair && (f.bn == 240 || f.persist) && g_cfg.split_k > 1)) c.tc = f;
     else c.kind = -1;
   }
   return c;
@@ -338,7 +340,7 @@ int pair_splits(const TcConfig &c, int64_t M, int64_t N, int64_t K) {
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     if (g_cfg.kernel == 3 && g_cfg.split_k > 0) return g_cfg.split_k;
   }
-  return c.bn == 256 ? auto_pair_splits(c.prec, M, N, K) : 1;
+  return c.bn == 256 && !c.persist ? auto_pair_splits(c.prec, M, N, K) : 1;
 }
 
 int auto_pair_splits(int prec, int64_t M, int64_t N, int64_t K) {
@@ -401,6 +403,11 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
       e = launch_splitk_reduce(epi, static_cast<const float *>(ws), splits, mp * a->N, a->M, a->N, a->bias, a->C_res,
                                a->out, ldc, st);
     cudaFreeAsync(ws, st);
+  } else if (cfg.persist) {
+    CUtensorMap tmO;
+    rc = make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 32, 128);
+    if (rc) return rc;
+    e = launch_gemm_pair_persistent(cfg.prec, cfg.stages, epi, tmA, tmB, tmO, p, st);
   } else if (cfg.pair) {
     CUtensorMap tmO, tmC;
     rc = make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 32, 128);
@@ -624,27 +631,38 @@ int tforge_describe(int workload, int64_t M, int64_t N, int64_t K, int mode, tfo
     return TFORGE_OK;
   }
   static const char *names[3] = {"tf_gemm_tcgen05_tf32", "tf_gemm_tcgen05_3xtf32", "tf_gemm_tcgen05_bf16"};
-  std::snprintf(out->kernel, sizeof(out->kernel), "%s%s", names[c.tc.prec], c.tc.pair ? "_pair" : "");
+  std::snprintf(out->kernel, sizeof(out->kernel), "%s%s", names[c.tc.prec],
+                c.tc.persist ? "_pair_persistent" : (c.tc.pair ? "_pair" : ""));
   const int tm = c.tc.pair ? 256 : 128;
   out->grid[0] = (int)((N + c.tc.bn - 1) / c.tc.bn) * (c.tc.pair ? 2 : 1);
   out->grid[1] = (int)((M + tm - 1) / tm);
   out->grid[2] = 1;
+  if (c.tc.persist) {  // one cluster per co-resident pair, each looping over tiles
+    const int64_t tiles = (int64_t)out->grid[0] / 2 * out->grid[1];
+    int pairs = have_dev ? persist_grid_pairs(c.tc.prec, c.tc.stages, epi, M, N) : -1;
+    if (pairs <= 0) pairs = (int)(tiles < device_pairs() ? tiles : device_pairs());
+    out->grid[0] = 2 * pairs;
+    out->grid[1] = 1;
+    out->persistent = 1;
+  }
   out->block[0] = c.tc.pair && c.tc.prec == PREC_X3 ? 384 : 256;  // 3xTF32 pair: 12 warps
   out->split_k = pair_splits(c.tc, M, N, K);
   out->grid[2] = out->split_k;
   out->block[1] = out->block[2] = 1;
   out->cluster[0] = c.tc.pair ? 2 : 1;
-  out->smem_bytes = c.tc.pair ? pair_smem_bytes(c.tc.prec, c.tc.stages) : tc_smem_bytes(c.tc);
+  out->smem_bytes = c.tc.persist ? persist_smem_bytes(c.tc.prec, c.tc.stages)
+                                  : (c.tc.pair ? pair_smem_bytes(c.tc.prec, c.tc.stages) : tc_smem_bytes(c.tc));
   out->tile[0] = tm;
   out->tile[1] = c.tc.bn;
   out->tile[2] = c.tc.prec == PREC_BF16 ? 64 : 32;
   out->stages = c.tc.stages;
-  out->tmem_cols = c.tc.pair ? pair_tmem_cols(c.tc.prec) : c.tc.bn;
+  out->tmem_cols = c.tc.persist ? 512 : (c.tc.pair ? pair_tmem_cols(c.tc.prec) : c.tc.bn);
   if (have_dev) {
     cudaFuncAttributes fa{};
     int blocks = 0;
-    cudaError_t e = c.tc.pair ? pair_func_attributes(c.tc.prec, c.tc.stages, c.tc.bn, epi, &fa, &blocks)
-                              : tc_func_attributes(c.tc, epi, &fa, &blocks);
+    cudaError_t e = c.tc.persist ? persist_func_attributes(c.tc.prec, c.tc.stages, epi, &fa, &blocks)
+                    : c.tc.pair  ? pair_func_attributes(c.tc.prec, c.tc.stages, c.tc.bn, epi, &fa, &blocks)
+                                 : tc_func_attributes(c.tc, epi, &fa, &blocks);
     fill_attrs(e, fa, blocks);
   }
   return TFORGE_OK;
@@ -656,7 +674,9 @@ int tforge_set_config(const tforge_config *cfg) {
     g_cfg = tforge_config{};
     return TFORGE_OK;
   }
-  if (cfg->kernel < 0 || cfg->kernel > 3 || cfg->split_k < 0 || cfg->split_k > 8) return TFORGE_ERR_MODE;
+  if (cfg->kernel < 0 || cfg->kernel > 3 || cfg->split_k < 0 || cfg->split_k > 8 || cfg->persistent < 0 ||
+      cfg->persistent > 1)
+    return TFORGE_ERR_MODE;
   g_cfg = *cfg;
   return TFORGE_OK;
 }

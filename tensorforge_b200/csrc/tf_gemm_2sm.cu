@@ -52,11 +52,6 @@
 
 namespace tf {
 
-#ifndef TF_RASTER_GROUP
-#define TF_RASTER_GROUP 8
-#endif
-// Tile rows per raster group of the pair kernel's launch order.
-constexpr int kRasterGroup = TF_RASTER_GROUP;
 
 namespace {
 
@@ -208,12 +203,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   // Grouped raster: launch order walks kRasterGroup tile rows at a time, column by column,
   // so the tiles of one wave share a few A row panels and B column panels in L2.
   const int tiles_n = (int)(gridDim.x >> 1), tiles_m = (int)gridDim.y;
-  const int pid = (int)blockIdx.y * tiles_n + (int)(blockIdx.x >> 1);
-  const int per_group = kRasterGroup * tiles_n, group = pid / per_group;
-  const int first_m = group * kRasterGroup;
-  const int group_m = tiles_m - first_m < kRasterGroup ? tiles_m - first_m : kRasterGroup;
-  const int tile_m = first_m + (pid - group * per_group) % group_m;
-  const int tile_n = (pid - group * per_group) / group_m;
+  int tile_m, tile_n;
+  raster_tile((int)blockIdx.y * tiles_n + (int)(blockIdx.x >> 1), tiles_m, tiles_n, kRasterGroup, tile_m, tile_n);
   const int n0 = tile_n * BN, m0 = tile_m * 256 + (int)rank * 128;
   // Split-K: this pair takes k-blocks [kb0, kb0 + nkb) of the tile's K and stores raw
   // partial sums at row offset blockIdx.z * split_rows of the output map.

@@ -25,6 +25,12 @@ constexpr int kPairSplit = TF_PAIR_SPLIT;
 // Landing-ring depth of the 3xTF32 pair kernel (its instantiated "stages").
 constexpr int kPairX3Land = TF_PAIR_X3_LAND;
 
+#ifndef TF_RASTER_GROUP
+#define TF_RASTER_GROUP 8
+#endif
+// Tile rows per raster group of the pair kernels' tile order.
+constexpr int kRasterGroup = TF_RASTER_GROUP;
+
 // Parameters of the tcgen05 kernel besides the two tensor maps.
 struct TcParams {
   const float *bias;   // N (mbr)
@@ -46,7 +52,8 @@ struct TcConfig {
   int prec;    // Prec
   int bn;      // 64, 128, 256 (output tile width; 256 for the CTA-pair kernel)
   int stages;
-  int pair;    // 1: CTA-pair kernel (cta_group::2, 256 x 256 tiles), 0: one CTA per 128 x bn tile
+  int pair;    // 1: CTA-pair kernel (cta_group::2, 256 x bn tiles), 0: one CTA per 128 x bn tile
+  int persist;  // 1 (pair, TF32 / BF16, bn 256): persistent pair kernel, two TMEM accumulators
 };
 
 // Dynamic shared memory the tcgen05 kernel needs for a configuration.
@@ -75,6 +82,17 @@ cudaError_t launch_gemm_pair(int prec, int stages, int bn, int epi, const CUtens
                              const TcParams &p, cudaStream_t stream);
 cudaError_t pair_func_attributes(int prec, int stages, int bn, int epi, cudaFuncAttributes *attr,
                                  int *blocks_per_sm);
+
+// Persistent CTA-pair kernel (TF32 / BF16 modes, 256 x 256 tiles, no split-K): clusters
+// loop over tiles with two TMEM accumulators.  tmO as for launch_gemm_pair; matmul_add reads
+// p.cres directly.  persist_grid_pairs: clusters it launches for M x N (-1 without a device).
+int persist_smem_bytes(int prec, int stages);
+cudaError_t launch_gemm_pair_persistent(int prec, int stages, int epi, const CUtensorMap &tmA,
+                                        const CUtensorMap &tmB, const CUtensorMap &tmO, const TcParams &p,
+                                        cudaStream_t stream);
+cudaError_t persist_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *attr,
+                                    int *blocks_per_sm);
+int persist_grid_pairs(int prec, int stages, int epi, int64_t M, int64_t N);
 
 // The dispatch table's tensor-core choice (false when it would not use tcgen05), the
 // TMA operand map encoder, and the per-thread error text (all defined in tf_api.cu).

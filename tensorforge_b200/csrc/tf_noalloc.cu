@@ -131,7 +131,8 @@ extern "C" int tforge_mbr_bf16_noalloc(const float *A, const float *B, const flo
     CUtensorMap tmO;
     rc = tf::encode_operand_map(&tmO, out, false, M, N, N, 32, 128, false);
     if (rc) return rc;
-    e = tf::launch_gemm_pair(cfg.prec, cfg.stages, cfg.bn, tf::EPI_MBR, tmA, tmB, tmO, tmO, p, st);
+    e = cfg.persist ? tf::launch_gemm_pair_persistent(cfg.prec, cfg.stages, tf::EPI_MBR, tmA, tmB, tmO, p, st)
+                    : tf::launch_gemm_pair(cfg.prec, cfg.stages, cfg.bn, tf::EPI_MBR, tmA, tmB, tmO, tmO, p, st);
   } else {
     e = tf::launch_gemm_tc(cfg, tf::EPI_MBR, tmA, tmB, p, st);
   }

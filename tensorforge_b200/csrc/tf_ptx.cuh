@@ -12,6 +12,18 @@ namespace tf {
 
 constexpr uint32_t kStatusTimeout = 6;  // == TFORGE_ERR_TIMEOUT
 
+// Grouped raster of a tiles_m x tiles_n tile grid: tile number `pid` walks `group` tile rows
+// at a time, column by column, so the tiles in flight share a few A row panels and B column
+// panels in L2.
+__device__ __forceinline__ void raster_tile(int pid, int tiles_m, int tiles_n, int group, int &tile_m,
+                                            int &tile_n) {
+  const int per_group = group * tiles_n, g = pid / per_group;
+  const int first_m = g * group;
+  const int group_m = tiles_m - first_m < group ? tiles_m - first_m : group;
+  tile_m = first_m + (pid - g * per_group) % group_m;
+  tile_n = (pid - g * per_group) / group_m;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -126,6 +138,10 @@ __device__ __forceinline__ void bulk_commit_group() {
 // Wait until every committed bulk store of this thread has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// The same, except that the most recently committed group may still be reading.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 // Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {

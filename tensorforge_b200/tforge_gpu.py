@@ -79,13 +79,13 @@ def parse_options(options: str) -> dict:
     opts = dict(o.split("=", 1) for o in options.split() if "=" in o)
     return {"precision": opts.get("precision", "fp32"), "bn": int(opts.get("bn", 0)),
             "stages": int(opts.get("stages", 0)), "kernel": opts.get("kernel", ""),
-            "split": int(opts.get("split", 0))}
+            "split": int(opts.get("split", 0)), "persistent": int(opts.get("persistent", 0))}
 
 
 def _forced_kind(o: dict) -> int:
     """tforge_config.kernel for parsed options: 0 table, 1 one-CTA, 2 SIMT, 3 CTA pair."""
     k = o.get("kernel", "")
-    if k == "pair" or (o.get("split") and not k):
+    if k == "pair" or ((o.get("split") or o.get("persistent")) and not k):
         return 3
     if k == "simt":
         return 2
@@ -108,7 +108,7 @@ def compile_kernel(workload, m, n, k, options="", tag="default"):
     d.mkdir(parents=True, exist_ok=True)
     kind = _forced_kind(o)
     if kind:
-        _lib.set_config(kind, o["bn"], o["stages"], split_k=o.get("split", 0))
+        _lib.set_config(kind, o["bn"], o["stages"], o.get("persistent", 0), o.get("split", 0))
     try:
         desc = _lib.describe(workload, m, n, k or 0, o["precision"])
     finally:
@@ -139,6 +139,8 @@ def _bench_cmd(workload, m, n, k, kdir=None, launch=None, mode="kernel"):
             cmd += ["--kernel", o["kernel"]]
         if o.get("split"):
             cmd += ["--split", o["split"]]
+        if o.get("persistent"):
+            cmd += ["--persistent"]
     return cmd
 
 
@@ -194,7 +196,7 @@ def run_op(workload: str, ins: dict, m: int, n: int, k: int | None, precision: s
     o = parse_options(options)
     kind = _forced_kind(o)
     if kind:
-        _lib.set_config(kind, o["bn"], o["stages"], split_k=o.get("split", 0))
+        _lib.set_config(kind, o["bn"], o["stages"], o.get("persistent", 0), o.get("split", 0))
     try:
         if workload in tc.GEMM_WORKLOADS:
             _lib.gemm(workload, bufs["a"].addr, bufs["b"].addr, out.addr, m, n, k, precision,

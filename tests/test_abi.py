@@ -129,7 +129,8 @@ def test_tuned_table_entries_are_what_dispatch_picks():
     for prec, m, n, k, pair, bn, stages, tflops in entries:
         assert tflops > 0
         d = _lib.describe("mbr", m, n, k, modes[prec])
-        assert d["kernel"].endswith("_pair") == bool(pair), (prec, m, n, k)
+        assert ("_pair" in d["kernel"]) == bool(pair), (prec, m, n, k)
+        assert d["kernel"].endswith("_pair_persistent") == (pair == 2), (prec, m, n, k)
         assert d["tile"][1] == bn, (prec, m, n, k)
         if not pair:  # the pair kernel has one instantiated depth per precision
             assert d["stages"] == stages
@@ -154,6 +155,18 @@ def test_forced_config_and_reset():
         _lib.set_config(3, 240, split_k=2)  # the 240-wide tile takes no split-K
         with pytest.raises(_lib.TforgeError):
             _lib.describe("mbr", 2048, 2048, 2048, "fp32")
+        _lib.set_config(3, 0, 0, 1)  # persistent pair kernel: TF32 / BF16 only
+        d = _lib.describe("mbr", 8192, 8192, 8192, "tf32")
+        assert d["kernel"] == "tf_gemm_tcgen05_tf32_pair_persistent" and d["persistent"] == 1
+        assert d["tmem_cols"] == 512 and d["grid"][1] == 1 and d["split_k"] == 1
+        assert d["grid"][0] == 148  # without a device: 74 SM pairs
+        d = _lib.describe("mbr", 300, 264, 64, "bf16")
+        assert d["kernel"] == "tf_gemm_tcgen05_bf16_pair_persistent" and d["grid"][0] == 8  # 2 x 2 tiles
+        with pytest.raises(_lib.TforgeError):
+            _lib.describe("mbr", 8192, 8192, 8192, "fp32")
+        _lib.set_config(3, 0, 0, 1, 2)  # no split-K either
+        with pytest.raises(_lib.TforgeError):
+            _lib.describe("mbr", 8192, 8192, 8192, "tf32")
     finally:
         _lib.set_config()
     assert _lib.describe("mbr", 2048, 2048, 2048, "tf32")["kernel"] == "tf_gemm_tcgen05_tf32_pair"

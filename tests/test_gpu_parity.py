@@ -341,6 +341,74 @@ def test_pair_kernel_bounded_wait(gpu):
             x.free()
 
 
+@pytest.mark.parametrize("mode", ["tf32", "bf16"])
+@pytest.mark.parametrize("workload", ["mbr", "matmul", "matmul_add"])
+@pytest.mark.parametrize("shape", [(2600, 2400, 96), (4100, 4000, 64), (300, 264, 520)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_persistent_pair_within_bound(gpu, workload, mode, shape):
+    """Persistent CTA-pair kernel: clusters loop over tiles with two TMEM accumulators
+    (110 and 272 tiles: every cluster reuses both accumulators; ragged M and N; one cluster
+    with a single ragged tile and a K tail)."""
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 31)
+    _lib.set_config(3, 0, 0, 1)
+    try:
+        d = _lib.describe(workload, m, n, k, mode)
+        assert d["kernel"].endswith("_pair_persistent") and d["persistent"] == 1 and d["tmem_cols"] == 512
+        tiles = -(-m // 256) * -(-n // 256)
+        assert d["grid"][0] == 2 * min(tiles, d["grid"][0] // 2) and d["grid"][1] == 1
+        out = tg.run_op(workload, ins, m, n, k, mode)
+    finally:
+        _lib.set_config()
+    res = tc.check_output(workload, ins, out, mode)
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+
+
+@pytest.mark.parametrize("mode", ["tf32", "bf16"])
+@pytest.mark.parametrize("workload", ["mbr", "matmul_add"])
+def test_persistent_pair_matches_pair_bitwise(gpu, workload, mode):
+    """Per tile the persistent kernel runs the pair kernel's k-block order and MMA sequence,
+    so the two agree bit for bit (160 tiles: two to three per cluster)."""
+    m, n, k = 4096, 2560, 256
+    ins = tc.make_inputs(workload, m, n, k, 37)
+    outs = []
+    for persistent in (0, 1):
+        _lib.set_config(3, 0, 0, persistent, 1)
+        try:
+            outs.append(tg.run_op(workload, ins, m, n, k, mode))
+        finally:
+            _lib.set_config()
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+
+
+def test_persistent_pair_bounded_wait(gpu):
+    """Timeout path of the persistent kernel: the MMA issuer, the producers and both CTAs'
+    epilogues give up, drain and meet; status is TIMEOUT; the next call is right."""
+    L = _lib.lib()
+    m, n, k = 1024, 1024, 256
+    ins = tc.make_inputs("mbr", m, n, k, 41)
+    a, b, bias = (tg.DeviceBuffer.upload(ins[x]) for x in ("a", "b", "bias"))
+    out = tg.DeviceBuffer(m * n * 4)
+    _lib.set_config(3, 0, 0, 1)
+    try:
+        for mode in ("tf32", "bf16"):
+            assert L.tforge_set_wait_limit_ns(50_000_000) == 0
+            assert L.tforge_debug_skip_load(1) == 0
+            try:
+                _lib.gemm("mbr", a.addr, b.addr, out.addr, m, n, k, mode, bias=bias.addr)
+                assert _lib.device_status(None) == _lib.ERR_TIMEOUT
+            finally:
+                L.tforge_debug_skip_load(0)
+                L.tforge_set_wait_limit_ns(0)
+            _lib.gemm("mbr", a.addr, b.addr, out.addr, m, n, k, mode, bias=bias.addr)
+            assert _lib.device_status(None) == 0
+            assert tc.check_output("mbr", ins, out.download((m, n)), mode)["pass"]
+    finally:
+        _lib.set_config()
+        for x in (a, b, bias, out):
+            x.free()
+
+
 def test_tf32_operands_are_read_truncated(gpu):
     """The truncation split of the 3xTF32 pair kernel relies on the tensor core reading an
     f32 operand as TF32 by discarding its low 13 mantissa bits (not rounding): pin it.
