@@ -230,9 +230,16 @@ int pair_width(int prec, int64_t M, int64_t N, int64_t K) {
   return w240 * 240 < w256 * 256 ? 240 : 256;
 }
 
-// Analytic fallback outside the measured range: the fewest waves over the tile area.
+// Analytic fallback outside the measured range: the fewest waves over the tile area.  The
+// pair kernel takes 256x240 tiles when they help (3xTF32, pair_width), or -- TF32 and BF16
+// with more tiles than SM pairs -- its persistent form, which overlaps each tile's epilogue
+// with the next tile's MMAs (it won every such shape of the tuning sweep but one, by 1 %).
 TcConfig model_tc(int prec, int64_t M, int64_t N, int64_t K) {
-  TcConfig best{prec, pair_width(prec, M, N, K), kStagesPair[prec], 1};
+  TcConfig best{prec, 256, kStagesPair[prec], 1, 0};
+  if (prec == PREC_X3)
+    best.bn = pair_width(prec, M, N, K);
+  else if (((M + 255) / 256) * ((N + 255) / 256) > device_pairs())
+    best.persist = 1;
   double best_cost = est_cost(M, N, 256, 256, 2, kKernelEff[0]);
   const int bns[3] = {256, 128, 64};
   for (int i = 0; i < 3; ++i) {
