@@ -234,11 +234,14 @@ int pair_width(int prec, int64_t M, int64_t N, int64_t K) {
 // pair kernel takes 256x240 tiles when they help (3xTF32, pair_width), or -- TF32 and BF16
 // with more tiles than SM pairs -- its persistent form, which overlaps each tile's epilogue
 // with the next tile's MMAs (it won every such shape of the tuning sweep but one, by 1 %).
+// Not beyond 32 tiles per pair: on a 131072 x 8192 x 8192 TF32 call (221 tiles per pair,
+// 30 ms under the power cap) the persistent kernel ran at a lower clock and 13 % slower.
 TcConfig model_tc(int prec, int64_t M, int64_t N, int64_t K) {
   TcConfig best{prec, 256, kStagesPair[prec], 1, 0};
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256), pairs = device_pairs();
   if (prec == PREC_X3)
     best.bn = pair_width(prec, M, N, K);
-  else if (((M + 255) / 256) * ((N + 255) / 256) > device_pairs())
+  else if (tiles > pairs && tiles <= 32 * pairs)
     best.persist = 1;
   double best_cost = est_cost(M, N, 256, 256, 2, kKernelEff[0]);
   const int bns[3] = {256, 128, 64};

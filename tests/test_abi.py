@@ -182,11 +182,13 @@ def test_model_picks_240_wide_pair_tiles_when_waves_allow():
 
 def test_model_picks_persistent_pair_for_multi_wave_tf32_bf16():
     """Outside the measured table, TF32 and BF16 shapes with more 256x256 tiles than SM
-    pairs take the persistent pair kernel (config 4's 131072 x 8192 x 8192, config 5's
-    layers on one GPU); one wave or fewer keeps the one-launch-per-tile pair kernel."""
+    pairs, up to 32 tiles per pair, take the persistent pair kernel; one wave or fewer, and
+    very long calls (config 4's 131072 x 8192 x 8192 on one GPU: 16384 tiles), keep the
+    one-launch-per-tile pair kernel."""
     for mode in ("tf32", "bf16"):
-        assert _lib.describe("mbr", 131072, 8192, 8192, mode)["kernel"].endswith("_pair_persistent")
-        assert _lib.describe("mbr", 65536, 16384, 4096, mode)["kernel"].endswith("_pair_persistent")
+        assert _lib.describe("mbr", 16384, 8192, 64, mode)["kernel"].endswith("_pair_persistent")  # 2048 tiles
+        assert _lib.describe("mbr", 131072, 8192, 8192, mode)["kernel"].endswith("_pair")
+        assert _lib.describe("mbr", 65536, 16384, 4096, mode)["kernel"].endswith("_pair")
     assert _lib.describe("mbr", 2048, 2048, 64, "tf32")["kernel"] == "tf_gemm_tcgen05_tf32_pair"
     assert _lib.describe("mbr", 131072, 8192, 8192, "fp32")["kernel"] == "tf_gemm_tcgen05_3xtf32_pair"
 
