@@ -72,7 +72,11 @@ enum tforge_dtype { TFORGE_F32 = 0, TFORGE_BF16 = 1 };
  * tforge-gpu-pipeline (lib/Transforms/Gpu.cpp:219-316) launched at
  * runners/gpu/tforge-gpu-bench.cu:292-302.  Pitches are in elements; 0 means packed
  * (lda = K, ldb = N, ldc = N; C_res shares ldc).  BF16 A/B are accepted only in
- * TFORGE_MODE_BF16 (inputs already converted, e.g. a weight converted once). */
+ * TFORGE_MODE_BF16 (inputs already converted, e.g. a weight converted once).
+ * out_dtype TFORGE_BF16 (TFORGE_MODE_BF16 only; not in tforge_gemm_host): out holds M x N
+ * bf16 values, the f32 results rounded to nearest even -- the same values tforge_convert_bf16
+ * of the f32 output gives, written without the f32 round trip (a hidden layer feeding a
+ * BF16-mode layer, e.g. the MLP chain's H). */
 typedef struct tforge_gemm_args {
   int32_t workload;      /* TFORGE_MATMUL, TFORGE_MBR or TFORGE_MATMUL_ADD */
   int32_t mode;          /* enum tforge_mode */
@@ -82,9 +86,10 @@ typedef struct tforge_gemm_args {
   const void *B;         /* K x N */
   const float *bias;     /* N        (mbr) */
   const float *C_res;    /* M x N    (matmul_add) */
-  float *out;            /* M x N */
+  void *out;             /* M x N, f32 (or bf16, see out_dtype) */
   int64_t M, N, K;
   int64_t lda, ldb, ldc;
+  int32_t out_dtype;     /* enum tforge_dtype; 0 = TFORGE_F32 */
 } tforge_gemm_args;
 
 int tforge_gemm(const tforge_gemm_args *args, void *stream);

@@ -26,7 +26,8 @@ class GemmArgs(C.Structure):
     _fields_ = [("workload", C.c_int32), ("mode", C.c_int32), ("a_dtype", C.c_int32),
                 ("b_dtype", C.c_int32), ("A", C.c_void_p), ("B", C.c_void_p), ("bias", C.c_void_p),
                 ("C_res", C.c_void_p), ("out", C.c_void_p), ("M", C.c_int64), ("N", C.c_int64),
-                ("K", C.c_int64), ("lda", C.c_int64), ("ldb", C.c_int64), ("ldc", C.c_int64)]
+                ("K", C.c_int64), ("lda", C.c_int64), ("ldb", C.c_int64), ("ldc", C.c_int64),
+                ("out_dtype", C.c_int32)]
 
 
 class Launch(C.Structure):
@@ -132,10 +133,11 @@ def set_config(kernel: int = 0, bn: int = 0, stages: int = 0, persistent: int = 
 
 def gemm(workload: str, A: int, B: int, out: int, M: int, N: int, K: int, mode: str = "fp32",
          bias: int | None = None, c_res: int | None = None, stream: int | None = None,
-         a_dtype: int = F32, b_dtype: int = F32, lda: int = 0, ldb: int = 0, ldc: int = 0) -> None:
+         a_dtype: int = F32, b_dtype: int = F32, lda: int = 0, ldb: int = 0, ldc: int = 0,
+         out_dtype: int = F32) -> None:
     """tforge_gemm on device pointers (ints), asynchronous on `stream`."""
     args = GemmArgs(WORKLOADS[workload], MODES[mode], a_dtype, b_dtype, A, B, bias, c_res, out,
-                    M, N, K, lda, ldb, ldc)
+                    M, N, K, lda, ldb, ldc, out_dtype)
     check(lib().tforge_gemm(C.byref(args), stream), f"tforge_gemm({workload}, {M}x{N}x{K}, {mode})")
 
 

@@ -57,7 +57,7 @@ EncodeTiledFn encode_fn() {
 // 128-byte swizzle (16-byte atoms, or 32-byte atoms with `atom32`, the layout the tensor
 // cores require for N-contiguous 32-bit operands); out-of-range elements read as zero.
 int make_tmap(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols, int64_t ld,
-              uint32_t box_cols, uint32_t box_rows, bool atom32 = false) {
+              uint32_t box_cols, uint32_t box_rows, bool atom32 = false, bool swizzle64 = false) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     g_last_error = "cuTensorMapEncodeTiled unavailable";
@@ -70,7 +70,8 @@ int make_tmap(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   swizzle64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                             : (atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B),
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -294,6 +295,8 @@ int check_gemm(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *l
     return TFORGE_ERR_MODE;
   if ((a->a_dtype == TFORGE_BF16 || a->b_dtype == TFORGE_BF16) && a->mode != TFORGE_MODE_BF16)
     return TFORGE_ERR_MODE;
+  if (a->out_dtype != TFORGE_F32 && !(a->out_dtype == TFORGE_BF16 && a->mode == TFORGE_MODE_BF16))
+    return TFORGE_ERR_MODE;
   if (a->M < 0 || a->N < 0 || a->K < 0) return TFORGE_ERR_SHAPE;
   if (a->M > INT32_MAX || a->N > INT32_MAX || a->K > INT32_MAX) return TFORGE_ERR_SHAPE;
   *lda = a->lda ? a->lda : a->K;
@@ -306,14 +309,15 @@ int check_gemm(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *l
   if (a->workload == TFORGE_MBR && !a->bias) return TFORGE_ERR_NULL;
   if (a->workload == TFORGE_MATMUL_ADD && !a->C_res) return TFORGE_ERR_NULL;
   const int ea = a->a_dtype == TFORGE_BF16 ? 2 : 4, eb = a->b_dtype == TFORGE_BF16 ? 2 : 4;
-  if (!aligned(a->A, ea) || !aligned(a->B, eb) || !aligned(a->out, 4) || !aligned(a->bias, 4) ||
+  const int eo = a->out_dtype == TFORGE_BF16 ? 2 : 4;
+  if (!aligned(a->A, ea) || !aligned(a->B, eb) || !aligned(a->out, eo) || !aligned(a->bias, 4) ||
       !aligned(a->C_res, 4))
     return TFORGE_ERR_ALIGN;
-  const size_t ob = span_bytes(a->M, a->N, *ldc, 4);
+  const size_t ob = span_bytes(a->M, a->N, *ldc, eo), cb = span_bytes(a->M, a->N, *ldc, 4);
   if (overlaps(a->out, ob, a->A, span_bytes(a->M, a->K, *lda, ea)) ||
       overlaps(a->out, ob, a->B, span_bytes(a->K, a->N, *ldb, eb)) ||
       (a->workload == TFORGE_MBR && overlaps(a->out, ob, a->bias, (size_t)a->N * 4)) ||
-      (a->workload == TFORGE_MATMUL_ADD && overlaps(a->out, ob, a->C_res, ob)))
+      (a->workload == TFORGE_MATMUL_ADD && overlaps(a->out, ob, a->C_res, cb)))
     return TFORGE_ERR_ALIAS;
   return TFORGE_OK;
 }
@@ -321,7 +325,8 @@ int check_gemm(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *l
 // TMA needs 16-byte-aligned bases and pitches; the vector epilogue needs 16-byte rows.
 bool tma_compatible(const tforge_gemm_args *a, int64_t lda, int64_t ldb, int64_t ldc) {
   const int ea = a->a_dtype == TFORGE_BF16 ? 2 : 4, eb = a->b_dtype == TFORGE_BF16 ? 2 : 4;
-  if ((lda * ea) % 16 || (ldb * eb) % 16 || (ldc * 4) % 16) return false;
+  const int eo = a->out_dtype == TFORGE_BF16 ? 2 : 4;
+  if ((lda * ea) % 16 || (ldb * eb) % 16 || (ldc * eo) % 16) return false;
   if (a->mode == TFORGE_MODE_BF16 && ((lda * 2) % 16 || (ldb * 2) % 16)) return false;
   if (!aligned(a->A, 16) || !aligned(a->B, 16) || !aligned(a->out, 16)) return false;
   if (a->workload == TFORGE_MBR && !aligned(a->bias, 16)) return false;
@@ -377,7 +382,9 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   TcParams p{};
   p.bias = a->bias;
   p.cres = a->C_res;
-  p.out = a->out;
+  p.out = static_cast<float *>(a->out);  // bf16 output (out_bf16) is written through tmO only
+  p.out_bf16 = a->out_dtype == TFORGE_BF16;
+  const bool ob16 = p.out_bf16 != 0;
   p.M = (int32_t)a->M;
   p.N = (int32_t)a->N;
   p.K = (int32_t)a->K;
@@ -411,16 +418,16 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
     e = launch_gemm_pair(cfg.prec, cfg.stages, cfg.bn, EPI_MATMUL, tmA, tmB, tmW, tmW, p, st);
     if (e == cudaSuccess)
       e = launch_splitk_reduce(epi, static_cast<const float *>(ws), splits, mp * a->N, a->M, a->N, a->bias, a->C_res,
-                               a->out, ldc, st);
+                               static_cast<float *>(a->out), ldc, st);
     cudaFreeAsync(ws, st);
   } else if (cfg.persist) {
     CUtensorMap tmO;
-    rc = make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 32, 128);
+    rc = make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, false, ob16);
     if (rc) return rc;
     e = launch_gemm_pair_persistent(cfg.prec, cfg.stages, epi, tmA, tmB, tmO, p, st);
   } else if (cfg.pair) {
     CUtensorMap tmO, tmC;
-    rc = make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 32, 128);
+    rc = make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, false, ob16);
     if (rc) return rc;
     tmC = tmO;
     if (a->workload == TFORGE_MATMUL_ADD) {
@@ -463,6 +470,33 @@ int device_pool(cudaMemPool_t *out) { return scratch_pool(out); }
 
 }  // namespace tf
 
+namespace {
+
+// bf16 output on a path without a bf16-output epilogue: the f32 result goes to pooled scratch
+// (packed), then one pass rounds it into out with the same conversion the epilogues use.
+int gemm_bf16_out_via_f32(const tforge_gemm_args *a, int64_t ldc, cudaStream_t st) {
+  cudaMemPool_t pool = nullptr;
+  int rc = scratch_pool(&pool);
+  if (rc) return rc;
+  void *tmp = nullptr;
+  cudaError_t e = cudaMallocFromPoolAsync(&tmp, sizeof(float) * (size_t)a->M * a->N, pool, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMallocFromPoolAsync(f32 output scratch)");
+  tforge_gemm_args t = *a;
+  t.out = tmp;
+  t.ldc = a->N;
+  t.out_dtype = TFORGE_F32;
+  rc = tforge_gemm(&t, st);
+  if (rc == TFORGE_OK) {
+    e = launch_convert_rows_bf16(static_cast<const float *>(tmp), a->N, static_cast<uint16_t *>(a->out), ldc, a->M,
+                                 a->N, st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "bf16 output conversion");
+  }
+  cudaFreeAsync(tmp, st);
+  return rc;
+}
+
+}  // namespace
+
 extern "C" {
 
 int tforge_gemm(const tforge_gemm_args *a, void *stream) {
@@ -475,11 +509,18 @@ int tforge_gemm(const tforge_gemm_args *a, void *stream) {
   const bool f32_in = a->a_dtype == TFORGE_F32 && a->b_dtype == TFORGE_F32;
   const Choice c = choose(a->mode, a->M, a->N, a->K, tma_compatible(a, lda, ldb, ldc));
   if (c.kind < 0) return TFORGE_ERR_UNSUPPORTED;
+  if (a->out_dtype == TFORGE_BF16) {
+    // Direct bf16 stores from the mbr epilogue of the 256-wide and persistent BF16 pair
+    // kernels (K and N multiples of 8 keep the bf16 operand rows TMA-aligned).
+    const bool direct = c.kind == K_TC && c.tc.prec == PREC_BF16 && epi == EPI_MBR &&
+                        (c.tc.persist || (c.tc.pair && c.tc.bn == 256)) && a->K % 8 == 0 && a->N % 8 == 0;
+    if (!direct) return gemm_bf16_out_via_f32(a, ldc, st);
+  }
   if (c.kind == K_SIMT) {
     if (!f32_in) return TFORGE_ERR_UNSUPPORTED;  // bf16 operands need the tensor-core path
     const float *aux = a->workload == TFORGE_MBR ? a->bias : a->C_res;
     cudaError_t e = launch_gemm_simt(epi, static_cast<const float *>(a->A),
-                                     static_cast<const float *>(a->B), aux, a->out, a->M, a->N, a->K,
+                                     static_cast<const float *>(a->B), aux, static_cast<float *>(a->out), a->M, a->N, a->K,
                                      lda, ldb, ldc, st);
     return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "SIMT GEMM launch");
   }
@@ -527,7 +568,7 @@ int tforge_gemm(const tforge_gemm_args *a, void *stream) {
     const float *aux = a->workload == TFORGE_MBR ? a->bias : a->C_res;
     if (!f32_in) return TFORGE_ERR_UNSUPPORTED;
     cudaError_t e = launch_gemm_simt(epi, static_cast<const float *>(a->A),
-                                     static_cast<const float *>(a->B), aux, a->out, a->M, a->N,
+                                     static_cast<const float *>(a->B), aux, static_cast<float *>(a->out), a->M, a->N,
                                      a->K, lda, ldb, ldc, st);
     return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "SIMT GEMM launch");
   }

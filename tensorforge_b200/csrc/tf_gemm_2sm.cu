@@ -64,6 +64,9 @@ constexpr int kPairOps = TF_PAIR_OPS;
 // 13 bits itself), so the MMAs read it from the landing slot and only B lo is written.
 constexpr bool kPairHiDirect = kPairSplit == 1;
 
+// bf16-output epilogue staging box: 128 rows x 32 bf16 columns.
+constexpr int kEpiBoxBytesB = 128 * 64;
+
 template <int PREC, int STAGES>
 struct PairLayout {
   // 3xTF32: warps 0 producer, 1 MMA (leader) / relay (peer), 2..11 converters.
@@ -163,7 +166,7 @@ __device__ __forceinline__ void relay_stages(uint32_t conv0, uint32_t ready0, ui
   }
 }
 
-template <int PREC, int STAGES, int EPI, int SPLIT, int BN>
+template <int PREC, int STAGES, int EPI, int SPLIT, int BN, bool OUTB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STAGES>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmC,
@@ -175,6 +178,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   // BN = 240: each CTA's MMA half is 120 B columns (the first 120 of the 128 it loads), and
   // the accumulator's last 32-column chunk holds only 16 output columns.
   static_assert(BN == 256 || BN == 240, "pair tile width");
+  // bf16 output (OUTB): BF16 precision, mbr epilogue, 256-wide tiles.
+  static_assert(!OUTB || (PREC == PREC_BF16 && EPI == EPI_MBR && BN == 256), "bf16 output configuration");
   constexpr int kHalfN = BN / 2;
   constexpr bool kHalfChunk = BN % 32 != 0;
 
@@ -509,6 +514,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
           }
           continue;  // every warp of this chunk takes this branch: no named barrier
         }
+        if constexpr (OUTB) {
+          // bf16 output: the chunk's 32 values of row r become 64 B in box c of 128 rows x
+          // 64 B (64-B swizzle: 16-B unit u of row r at unit u ^ ((r >> 1) & 3), matching the
+          // bf16 output map), stored by TMA like the f32 boxes.
+          uint8_t *bbox = smem + c * kEpiBoxBytesB + r * 64;
+          if (res_ok && cta_rows && col0 < p.N) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float4 v0 = finish(2 * u), v1 = finish(2 * u + 1);
+              uint4 pk;
+              pk.x = pack_bf16x2(v0.x, v0.y);
+              pk.y = pack_bf16x2(v0.z, v0.w);
+              pk.z = pack_bf16x2(v1.x, v1.y);
+              pk.w = pack_bf16x2(v1.z, v1.w);
+              *reinterpret_cast<uint4 *>(bbox + ((u ^ ((r >> 1) & 3)) << 4)) = pk;
+            }
+          }
+          fence_proxy_async_smem();
+          named_barrier(1 + c, 128);
+          if (q == 0 && lane == 0 && res_ok && cta_rows && col0 < p.N) {
+            tma_store_2d(&tmO, sbase + c * kEpiBoxBytesB, col0, out_row0);
+            bulk_commit_group();
+          }
+          continue;
+        }
         if (res_ok && cta_rows && col0 < p.N) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) *reinterpret_cast<float4 *>(box + ((j ^ (r & 7)) << 4)) = finish(j);
@@ -533,13 +563,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   }
 }
 
-template <int PREC, int STAGES, int EPI, int BN>
-cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
-                            const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
+template <int PREC, int STAGES, int EPI, int BN, bool OUTB>
+cudaError_t launch_pair_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
+                             const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   using L = PairLayout<PREC, STAGES>;
-  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit, BN>;
-  // The 240-wide tile stores its last 16 columns through p.out, so it takes no split-K.
-  if (BN != 256 && p.splits > 1) return cudaErrorInvalidValue;
+  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit, BN, OUTB>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -552,6 +580,20 @@ cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, cons
   dim3 grid(2 * ((p.N + BN - 1) / BN), (p.M + 255) / 256, p.splits > 1 ? p.splits : 1);
   kern<<<grid, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, tmO, tmC, p);
   return cudaGetLastError();
+}
+
+template <int PREC, int STAGES, int EPI, int BN>
+cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
+                            const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
+  // The 240-wide tile stores its last 16 columns through p.out, so it takes no split-K.
+  if (BN != 256 && p.splits > 1) return cudaErrorInvalidValue;
+  if (p.out_bf16) {
+    if constexpr (PREC == PREC_BF16 && EPI == EPI_MBR && BN == 256)
+      return p.splits > 1 ? cudaErrorInvalidValue
+                          : launch_pair_kern<PREC, STAGES, EPI, BN, true>(tmA, tmB, tmO, tmC, p, stream);
+    return cudaErrorInvalidValue;
+  }
+  return launch_pair_kern<PREC, STAGES, EPI, BN, false>(tmA, tmB, tmO, tmC, p, stream);
 }
 
 template <int PREC, int STAGES, int BN>
@@ -568,9 +610,9 @@ cudaError_t launch_pair_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &
 template <int PREC, int STAGES, int BN>
 cudaError_t pair_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
   using L = PairLayout<PREC, STAGES>;
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit, BN>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit, BN>)
-                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit, BN>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit, BN, false>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit, BN, false>)
+                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit, BN, false>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);

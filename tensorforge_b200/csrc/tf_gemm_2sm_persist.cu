@@ -64,13 +64,15 @@ __device__ __forceinline__ void pause_ns(uint64_t ns) {
   while (globaltimer() - t0 < ns) __nanosleep(1000);
 }
 
-template <int PREC, int STAGES, int EPI>
+template <int PREC, int STAGES, int EPI, bool OUTB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 const __grid_constant__ CUtensorMap tmO, const TcParams p) {
   using L = PersistLayout<PREC, STAGES>;
   constexpr bool kTF32 = PREC == PREC_TF32;
   constexpr uint32_t kIdesc = instr_desc(kTF32 ? 2u : 1u, 256, 256);
+  // bf16 output (OUTB): BF16 precision and the mbr epilogue only.
+  static_assert(!OUTB || (PREC == PREC_BF16 && EPI == EPI_MBR), "bf16 output configuration");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -244,7 +246,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         uint8_t *box = boxes + (c & 1) * L::kBoxBytes;
         if (et == 0) bulk_wait_group_read1();
         named_barrier(2, 128);
-        if (live) {
+        if (OUTB && live) {
+          // bf16 output: 64 B per row in the box's first 8 KB (64-B swizzle: 16-B unit u of
+          // row r at unit u ^ ((r >> 1) & 3)), matching the bf16 output map.
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float4 bb = bias_s[c * 8 + 2 * u + h];
+              const int e = 8 * u + 4 * h;
+              pk[2 * h] = pack_bf16x2(relu_ieee(__fadd_rn(__uint_as_float(rr[e]), bb.x)),
+                                      relu_ieee(__fadd_rn(__uint_as_float(rr[e + 1]), bb.y)));
+              pk[2 * h + 1] = pack_bf16x2(relu_ieee(__fadd_rn(__uint_as_float(rr[e + 2]), bb.z)),
+                                          relu_ieee(__fadd_rn(__uint_as_float(rr[e + 3]), bb.w)));
+            }
+            *reinterpret_cast<uint4 *>(box + r * 64 + ((u ^ ((r >> 1) & 3)) << 4)) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+        } else if (live) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float4 v = make_float4(__uint_as_float(rr[4 * j]), __uint_as_float(rr[4 * j + 1]),
@@ -289,10 +309,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 }
 
 // Co-resident clusters of one instantiation on the current device (0 on failure).
-template <int PREC, int STAGES, int EPI>
+template <int PREC, int STAGES, int EPI, bool OUTB = false>
 int persist_clusters() {
   using L = PersistLayout<PREC, STAGES>;
-  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI>;
+  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB>;
   static int cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -327,17 +347,29 @@ int persist_clusters() {
   return n;
 }
 
-template <int PREC, int STAGES, int EPI>
-cudaError_t launch_persist_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
-                               const TcParams &p, cudaStream_t stream) {
+template <int PREC, int STAGES, int EPI, bool OUTB>
+cudaError_t launch_persist_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
+                                const TcParams &p, cudaStream_t stream) {
   using L = PersistLayout<PREC, STAGES>;
-  if (p.splits > 1) return cudaErrorInvalidValue;
-  const int clusters = persist_clusters<PREC, STAGES, EPI>();
+  const int clusters = persist_clusters<PREC, STAGES, EPI, OUTB>();
   if (clusters <= 0) return cudaErrorInvalidConfiguration;
   const int64_t tiles = (int64_t)((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int pairs = tiles < clusters ? (int)tiles : clusters;
-  gemm_pair_persistent_kernel<PREC, STAGES, EPI><<<2 * pairs, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, tmO, p);
+  gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB><<<2 * pairs, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB,
+                                                                                                       tmO, p);
   return cudaGetLastError();
+}
+
+template <int PREC, int STAGES, int EPI>
+cudaError_t launch_persist_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
+                               const TcParams &p, cudaStream_t stream) {
+  if (p.splits > 1) return cudaErrorInvalidValue;
+  if (p.out_bf16) {
+    if constexpr (PREC == PREC_BF16 && EPI == EPI_MBR)
+      return launch_persist_kern<PREC, STAGES, EPI, true>(tmA, tmB, tmO, p, stream);
+    return cudaErrorInvalidValue;
+  }
+  return launch_persist_kern<PREC, STAGES, EPI, false>(tmA, tmB, tmO, p, stream);
 }
 
 template <int PREC, int STAGES>
@@ -354,9 +386,9 @@ cudaError_t launch_persist_epi(int epi, const CUtensorMap &tmA, const CUtensorMa
 template <int PREC, int STAGES>
 cudaError_t persist_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
   using L = PersistLayout<PREC, STAGES>;
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MBR>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_ADD>)
-                                   : reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MATMUL>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MBR, false>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_ADD, false>)
+                                   : reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MATMUL, false>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);

@@ -76,6 +76,7 @@ extern "C" int tforge_gemm_host(const tforge_gemm_args *a, int64_t chunk_rows, v
   int64_t lda, ldb, ldc;
   int rc = tf::check_gemm_args(a, &lda, &ldb, &ldc);
   if (rc) return rc;
+  if (a->out_dtype != TFORGE_F32) return TFORGE_ERR_MODE;  // host buffers: f32 output only
   if (a->M == 0 || a->N == 0) return TFORGE_OK;
   const int64_t M = a->M, N = a->N, K = a->K;
   const size_t ea = a->a_dtype == TFORGE_BF16 ? 2 : 4, eb = a->b_dtype == TFORGE_BF16 ? 2 : 4;
@@ -161,7 +162,7 @@ extern "C" int tforge_gemm_host(const tforge_gemm_args *a, int64_t chunk_rows, v
     e = cudaEventRecord(c.computed[i], cs);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(c.d2h, c.computed[i], 0);
     if (e == cudaSuccess)
-      e = cudaMemcpy2DAsync(a->out + (size_t)r0 * ldc, ldc * 4, base + oOut + (size_t)r0 * N * 4, N * 4, N * 4,
+      e = cudaMemcpy2DAsync(static_cast<float *>(a->out) + (size_t)r0 * ldc, ldc * 4, base + oOut + (size_t)r0 * N * 4, N * 4, N * 4,
                             nr, cudaMemcpyDeviceToHost, c.d2h);
     if (e != cudaSuccess) rc = fail(e, "tforge_gemm_host: out copy-back");
   }

@@ -46,6 +46,10 @@ struct TcParams {
   // z * split_rows; 0 or 1 = no split.
   int32_t splits;
   int32_t split_rows;
+  // 1: out holds bf16 (RNE of the f32 results), tmO is a bf16 map (box 32 columns x 128
+  // rows, 64-B swizzle).  BF16 precision, mbr epilogue, 256-wide pair tiles or the
+  // persistent pair kernel only.
+  int32_t out_bf16;
 };
 
 struct TcConfig {
@@ -97,6 +101,9 @@ int persist_grid_pairs(int prec, int stages, int epi, int64_t M, int64_t N);
 // The dispatch table's tensor-core choice (false when it would not use tcgen05), the
 // TMA operand map encoder, and the per-thread error text (all defined in tf_api.cu).
 bool select_tc_config(int mode, int64_t M, int64_t N, int64_t K, TcConfig *out);
+// dst[r * ldd + c] = bf16_rn(src[r * lds + c]) for r < M, c < N.
+cudaError_t launch_convert_rows_bf16(const float *src, int64_t lds, uint16_t *dst, int64_t ldd, int64_t M,
+                                     int64_t N, cudaStream_t stream);
 int encode_operand_map(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols,
                        int64_t ld, uint32_t box_cols, uint32_t box_rows, bool atom32);
 void set_last_error(const char *msg);

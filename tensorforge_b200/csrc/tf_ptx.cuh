@@ -379,6 +379,13 @@ __host__ __device__ constexpr uint32_t instr_desc(uint32_t fmt, uint32_t m, uint
          ((m >> 4) << 24);
 }
 
+// Two f32 values rounded to nearest-even bf16, packed: lo in bits [0, 16), hi in [16, 32).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
 // IEEE-2019 maximum(x, +0.0): a NaN input is returned unchanged (payload kept, as the
 // reference's fold keeps 0x7FC00000, test/Transforms/canonicalize.mlir:90-100), -0.0 and
 // negatives give +0.0.  Written on the bit pattern: a float compare-and-select may be

@@ -196,6 +196,16 @@ __global__ void convert_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *
     y[i] = __float2bfloat16_rn(x[i]);
 }
 
+// Pitched f32 -> bf16 rows (one element per thread step; the general bf16-output path).
+__global__ void convert_rows_bf16_kernel(const float *__restrict__ x, int64_t lds, __nv_bfloat16 *__restrict__ y,
+                                         int64_t ldd, int64_t M, int64_t N) {
+  const int64_t total = M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / N, c = i - r * N;
+    y[r * ldd + c] = __float2bfloat16_rn(x[r * lds + c]);
+  }
+}
+
 int grid_for(int64_t work, int threads) {
   // Grid-stride loops: enough CTAs to fill 148 SMs several times over.
   int64_t g = (work + threads - 1) / threads;
@@ -283,6 +293,14 @@ cudaError_t launch_elementwise(int op, const float *X, const float *Y, float *Z,
   } else {
     elementwise_scalar<<<grid_for(n, 256), 256, 0, stream>>>(op, X, Y, Z, n, N);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_convert_rows_bf16(const float *src, int64_t lds, uint16_t *dst, int64_t ldd, int64_t M,
+                                     int64_t N, cudaStream_t stream) {
+  if (M == 0 || N == 0) return cudaSuccess;
+  convert_rows_bf16_kernel<<<grid_for(M * N, 256), 256, 0, stream>>>(src, lds, reinterpret_cast<__nv_bfloat16 *>(dst),
+                                                                     ldd, M, N);
   return cudaGetLastError();
 }
 

@@ -2,8 +2,10 @@
 
 The direct consumer of the fused dense layer: layer 1 writes H into a caller-owned buffer,
 layer 2 reads it; nothing else is materialised.  In BF16 mode the weights are rounded to
-bf16 once (tforge_convert_bf16) and passed as bf16 operands, so only the activations are
-converted per call.  Rows of X shard over GPUs like tensorforge_b200.shard: weights are
+bf16 once (tforge_convert_bf16) and passed as bf16 operands, and H is kept in bf16 by
+default: layer 1's epilogue rounds its output to bf16 (out_dtype = TFORGE_BF16), which is
+exactly what layer 2 would do to an f32 H before its MMAs, so the result is the same bits
+with half the H traffic and no conversion pass (`--h-dtype f32` keeps an f32 H).  Rows of X shard over GPUs like tensorforge_b200.shard: weights are
 broadcast once, H and the output stay on the rank that owns the rows.
 
     python -m tensorforge_b200.mlp --shape 65536x4096x16384 --mode fp32        # one GPU
@@ -24,10 +26,14 @@ from .shard import broadcast_weights, row_partition
 class MLP2:
     """relu(relu(X @ W1 + b1) @ W2 + b2) on torch tensors of one GPU, through the C-ABI."""
 
-    def __init__(self, w1, b1, w2, b2, mode: str = "fp32"):
+    def __init__(self, w1, b1, w2, b2, mode: str = "fp32", h_bf16: bool | None = None):
         import torch
 
         self.mode = mode
+        # BF16 mode: H in bf16 unless asked otherwise; other modes keep an f32 H.
+        self.h_bf16 = (mode == "bf16") if h_bf16 is None else bool(h_bf16)
+        if self.h_bf16 and mode != "bf16":
+            raise ValueError("a bf16 H needs mode='bf16'")
         self.b1, self.b2 = b1, b2
         self.d, self.h = w1.shape
         if w2.shape != (self.h, self.d) or b1.shape != (self.h,) or b2.shape != (self.d,):
@@ -45,18 +51,27 @@ class MLP2:
             self.w1, self.w2 = w1, w2
             self.b_dtype = _lib.F32
 
+    @property
+    def h_dtype(self):
+        import torch
+
+        return torch.bfloat16 if self.h_bf16 else torch.float32
+
     def layer(self, x, w, b, out, stream) -> None:
+        import torch
+
         m, k = x.shape
         n = w.shape[1]
+        dt = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
         _lib.gemm("mbr", x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, k, self.mode, bias=b.data_ptr(),
-                  stream=stream, a_dtype=_lib.F32, b_dtype=self.b_dtype)
+                  stream=stream, a_dtype=dt[x.dtype], b_dtype=self.b_dtype, out_dtype=dt[out.dtype])
 
     def __call__(self, x, h=None, out=None, stream=None):
         import torch
 
         m = x.shape[0]
         if h is None:
-            h = torch.empty((m, self.h), device=x.device, dtype=torch.float32)
+            h = torch.empty((m, self.h), device=x.device, dtype=self.h_dtype)
         if out is None:
             out = torch.empty((m, self.d), device=x.device, dtype=torch.float32)
         if stream is None:
@@ -85,6 +100,8 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--check-rows", type=int, default=16, help="rows checked against FP64 per layer")
+    ap.add_argument("--h-dtype", default="auto", choices=["auto", "f32", "bf16"],
+                    help="hidden activation storage (auto: bf16 in BF16 mode, else f32)")
     args = ap.parse_args(argv)
     args.m, args.d, args.h = (int(x) for x in args.shape.lower().split("x"))
 
@@ -117,8 +134,8 @@ def main(argv=None) -> int:
         b2.normal_(0.0, 0.02, generator=g0)
     broadcast_weights(w1, b1)
     broadcast_weights(w2, b2)
-    model = MLP2(w1, b1, w2, b2, args.mode)
-    h = torch.empty((rows, args.h), device=dev)
+    model = MLP2(w1, b1, w2, b2, args.mode, None if args.h_dtype == "auto" else args.h_dtype == "bf16")
+    h = torch.empty((rows, args.h), device=dev, dtype=model.h_dtype)
     out = torch.empty((rows, args.d), device=dev)
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
@@ -139,8 +156,9 @@ def main(argv=None) -> int:
 
     # Per-layer FP64 check on a seeded subset of this rank's rows (layer 2 on our own H).
     sel = np.sort(np.random.default_rng(rank).choice(rows, min(args.check_rows, rows), replace=False))
-    xs, hs, os_ = x[sel].cpu().numpy(), h[sel].cpu().numpy(), out[sel].cpu().numpy()
-    r_1 = tc.check_output("mbr", {"a": xs, "b": w1.cpu().numpy(), "bias": b1.cpu().numpy()}, hs, args.mode)
+    xs, hs, os_ = x[sel].cpu().numpy(), h[sel].float().cpu().numpy(), out[sel].cpu().numpy()
+    r_1 = tc.check_output("mbr", {"a": xs, "b": w1.cpu().numpy(), "bias": b1.cpu().numpy()}, hs, args.mode,
+                          out_unit=2.0 ** -8 if model.h_bf16 else 0.0)
     r_2 = tc.check_output("mbr", {"a": hs, "b": w2.cpu().numpy(), "bias": b2.cpu().numpy()}, os_, args.mode)
     ok = torch.tensor([int(r_1["pass"] and r_2["pass"] and status == 0)], device=dev)
     if world > 1:
@@ -148,7 +166,8 @@ def main(argv=None) -> int:
     if rank == 0:
         t = float(ms.item())
         print(json.dumps({"workload": f"mlp2 X {args.m}x{args.d}, W1 {args.d}x{args.h}, W2 {args.h}x{args.d}",
-                          "mode": args.mode, "n_gpus": world, "ms_per_step": t,
+                          "mode": args.mode, "h_dtype": "bf16" if model.h_bf16 else "f32",
+                          "n_gpus": world, "ms_per_step": t,
                           "tflops": flops(args.m, args.d, args.h) / (t * 1e-3) / 1e12,
                           "err_over_bound_layer1": r_1["err_over_bound"], "err_over_bound_layer2": r_2["err_over_bound"],
                           "checked_rows_per_rank": int(len(sel)), "pass": bool(ok.item())}), flush=True)

@@ -101,8 +101,11 @@ def error_bound(mag, k: int, workload: str, mode: str = "fp32", ab_mag=None):
     return bound
 
 
-def check_output(workload: str, ins: dict, out: np.ndarray, mode: str = "fp32", rows=None) -> dict:
-    """Reference FP64 check of a GEMM output (optionally on a row subset)."""
+def check_output(workload: str, ins: dict, out: np.ndarray, mode: str = "fp32", rows=None,
+                 out_unit: float = 0.0) -> dict:
+    """Reference FP64 check of a GEMM output (optionally on a row subset).  `out_unit` is the
+    unit roundoff of an output stored below f32 precision (2^-8 for a bf16 output rounded to
+    nearest): the bound grows by out_unit * |ref|."""
     k = ins["a"].shape[1]
     o = out if rows is None else out[rows]
     ref, mag = reference64(workload, ins, rows)
@@ -111,13 +114,16 @@ def check_output(workload: str, ins: dict, out: np.ndarray, mode: str = "fp32", 
         a = ins["a"] if rows is None else ins["a"][rows]
         ab_mag = np.abs(a.astype(np.float64)) @ np.abs(ins["b"].astype(np.float64))
     bound = error_bound(mag, k, workload, mode, ab_mag)
+    if out_unit:
+        bound = bound + out_unit * np.abs(ref)
     err = np.abs(o.astype(np.float64) - ref)
     res = {"nan_count": int(np.isnan(o).sum()),
            "max_abs_err": float(np.nanmax(err)) if err.size else 0.0,
            "err_over_bound": float(np.nanmax(err / bound)) if err.size else 0.0,
            "rms_err": float(np.sqrt(np.nanmean(err ** 2))) if err.size else 0.0,
            "tolerance": (f"gamma_{k + (workload != 'matmul')}*(|A||B|+|aux|)" +
-                         (f" + (2u+u^2)|A||B|, u={INPUT_UNIT[mode]:.3g}" if INPUT_UNIT[mode] else ""))}
+                         (f" + (2u+u^2)|A||B|, u={INPUT_UNIT[mode]:.3g}" if INPUT_UNIT[mode] else "") +
+                         (f" + {out_unit:.3g}|ref|" if out_unit else ""))}
     res["pass"] = res["nan_count"] == int(np.isnan(ref).sum()) and res["err_over_bound"] <= 1.0
     return res
 

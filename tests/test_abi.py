@@ -68,6 +68,20 @@ def test_bf16_operands_need_bf16_mode():
     assert _lib.lib().tforge_gemm(C.byref(args), None) == _lib.ERR_MODE
 
 
+def test_bf16_output_needs_bf16_mode_and_device_buffers():
+    """out_dtype = TFORGE_BF16 is a BF16-mode option of tforge_gemm; other modes, unknown
+    dtypes and the host-buffer entry reject it before any CUDA call."""
+    L = _lib.lib()
+    for mode, out_dtype in ((0, _lib.BF16), (1, _lib.BF16), (2, 7)):  # fp32, tf32, bad dtype
+        args = _lib.GemmArgs(0, mode, _lib.F32, _lib.F32, P, 2 * P, None, None, 4 * P, 8, 8, 8, 0, 0, 0, out_dtype)
+        assert L.tforge_gemm(C.byref(args), None) == _lib.ERR_MODE
+    args = _lib.GemmArgs(0, 2, _lib.F32, _lib.F32, P, 2 * P, None, None, 4 * P, 8, 8, 8, 0, 0, 0, _lib.BF16)
+    assert L.tforge_gemm_host(C.byref(args), 0, None) == _lib.ERR_MODE
+    # An odd out address is misaligned for bf16 as well as f32.
+    args = _lib.GemmArgs(0, 2, _lib.F32, _lib.F32, P, 2 * P, None, None, 4 * P + 1, 8, 8, 8, 0, 0, 0, _lib.BF16)
+    assert L.tforge_gemm(C.byref(args), None) == _lib.ERR_ALIGN
+
+
 def test_pitch_smaller_than_row_is_rejected():
     args = _lib.GemmArgs(0, 0, _lib.F32, _lib.F32, P, 2 * P, None, None, 4 * P, 8, 8, 8, 4, 0, 0)
     assert _lib.lib().tforge_gemm(C.byref(args), None) == _lib.ERR_SHAPE

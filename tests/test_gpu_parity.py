@@ -468,10 +468,74 @@ def test_mlp_chain_per_layer_bound(gpu, mode):
     h, out = model(t["x"])
     torch.cuda.synchronize()
     assert _lib.device_status(None) == 0
-    hn, on = h.cpu().numpy(), out.cpu().numpy()
-    r1 = tc.check_output("mbr", {"a": ins["x"], "b": ins["w1"], "bias": ins["b1"]}, hn, mode)
+    assert model.h_bf16 == (mode == "bf16")  # BF16 mode keeps H in bf16 by default
+    hn, on = h.float().cpu().numpy(), out.cpu().numpy()
+    r1 = tc.check_output("mbr", {"a": ins["x"], "b": ins["w1"], "bias": ins["b1"]}, hn, mode,
+                         out_unit=2.0 ** -8 if model.h_bf16 else 0.0)
     r2 = tc.check_output("mbr", {"a": hn, "b": ins["w2"], "bias": ins["b2"]}, on, mode)
     assert r1["pass"] and r2["pass"], (r1, r2)
+
+
+def test_mlp_bf16_h_matches_f32_h_bitwise(gpu):
+    """A bf16 H (layer 1 rounds in its epilogue) gives the same H values as rounding an f32
+    H, and the same final output bits (layer 2 rounds an f32 H to bf16 before its MMAs)."""
+    import torch
+    from tensorforge_b200.mlp import MLP2
+
+    ins = tc.make_mlp_inputs(1100, 512, 2048, seed=8)
+    dev = torch.device("cuda", 0)
+    t = {k: torch.from_numpy(v).to(dev) for k, v in ins.items()}
+    h16, out16 = MLP2(t["w1"], t["b1"], t["w2"], t["b2"], "bf16", h_bf16=True)(t["x"])
+    h32, out32 = MLP2(t["w1"], t["b1"], t["w2"], t["b2"], "bf16", h_bf16=False)(t["x"])
+    torch.cuda.synchronize()
+    assert h16.dtype == torch.bfloat16 and h32.dtype == torch.float32
+    ref16 = torch.empty_like(h16)
+    _lib.check(_lib.lib().tforge_convert_bf16(h32.data_ptr(), ref16.data_ptr(), h32.numel(), None), "convert")
+    torch.cuda.synchronize()
+    assert torch.equal(h16.view(torch.int16), ref16.view(torch.int16))
+    assert torch.equal(out16.view(torch.int32), out32.view(torch.int32))
+
+
+@pytest.mark.parametrize("case", [
+    ("mbr", 2048, 2048, 512, 0, None),          # pair kernel, bf16 epilogue
+    ("mbr", 1000, 2048, 512, 8, None),          # ragged M, pitched out
+    ("mbr", 2600, 2400, 96, 0, (3, 0, 0, 1)),   # persistent pair kernel, 110 tiles
+    ("mbr", 300, 264, 520, 0, (3, 0, 0, 1)),    # persistent, one ragged tile, K tail
+    ("mbr", 256, 256, 128, 0, None),            # one-CTA kernel: f32 scratch then rounded
+    ("mbr", 300, 1004, 64, 0, None),            # N % 8 != 0: f32 scratch path
+    ("matmul", 1024, 1024, 256, 0, None),       # matmul: f32 scratch path
+    ("matmul_add", 512, 768, 128, 0, None),
+], ids=lambda c: f"{c[0]}-{c[1]}x{c[2]}x{c[3]}-ld{c[4]}-{'forced' if c[5] else 'table'}")
+def test_bf16_output_matches_f32_then_convert(gpu, case):
+    """out_dtype = TFORGE_BF16: the bf16 output equals tforge_convert_bf16 of the f32 output
+    bit for bit, on the direct epilogue paths and the f32-scratch ones; a NaN row too."""
+    import torch
+
+    wl, m, n, k, pad, cfg = case
+    ins = tc.make_inputs(wl, m, n, k, 43)
+    ins["a"][0, 0] = np.nan
+    dev = torch.device("cuda", 0)
+    t = {name: torch.from_numpy(arr).to(dev) for name, arr in ins.items()}
+    ldc = n + pad
+    out32 = torch.empty((m, n), device=dev)
+    out16 = torch.full((m, ldc), 7.0, device=dev, dtype=torch.bfloat16)
+    if cfg:
+        _lib.set_config(*cfg)
+    try:
+        for out, od, ld in ((out32, _lib.F32, 0), (out16, _lib.BF16, ldc)):
+            _lib.gemm(wl, t["a"].data_ptr(), t["b"].data_ptr(), out.data_ptr(), m, n, k, "bf16",
+                      bias=t["bias"].data_ptr() if "bias" in t else None,
+                      c_res=t["c"].data_ptr() if "c" in t else None, ldc=ld, out_dtype=od)
+    finally:
+        _lib.set_config()
+    ref = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+    _lib.check(_lib.lib().tforge_convert_bf16(out32.data_ptr(), ref.data_ptr(), m * n, None), "convert")
+    torch.cuda.synchronize()
+    assert _lib.device_status(None) == 0
+    assert torch.equal(out16[:, :n].contiguous().view(torch.int16), ref.view(torch.int16))
+    if pad:
+        assert bool((out16[:, n:] == 7.0).all())  # the pitch's padding is untouched
+    assert bool(torch.isnan(out16[0, :n].float()).all())
 
 
 def test_concurrent_streams_match_single_stream(gpu):
