@@ -513,7 +513,8 @@ int tforge_gemm(const tforge_gemm_args *a, void *stream) {
     // Direct bf16 stores from the mbr epilogue of the 256-wide and persistent BF16 pair
     // kernels (K and N multiples of 8 keep the bf16 operand rows TMA-aligned).
     const bool direct = c.kind == K_TC && c.tc.prec == PREC_BF16 && epi == EPI_MBR &&
-                        (c.tc.persist || (c.tc.pair && c.tc.bn == 256)) && a->K % 8 == 0 && a->N % 8 == 0;
+                        (c.tc.persist || (c.tc.pair && c.tc.bn == 256)) && a->K % 8 == 0 && a->N % 8 == 0 &&
+                        pair_splits(c.tc, a->M, a->N, a->K) <= 1;  // a forced split-K reduces in f32
     if (!direct) return gemm_bf16_out_via_f32(a, ldc, st);
   }
   if (c.kind == K_SIMT) {

@@ -505,6 +505,7 @@ def test_mlp_bf16_h_matches_f32_h_bitwise(gpu):
     ("mbr", 300, 1004, 64, 0, None),            # N % 8 != 0: f32 scratch path
     ("matmul", 1024, 1024, 256, 0, None),       # matmul: f32 scratch path
     ("matmul_add", 512, 768, 128, 0, None),
+    ("mbr", 512, 512, 2048, 0, (3, 0, 0, 0, 2)),  # forced split-K: f32 reduction, then rounded
 ], ids=lambda c: f"{c[0]}-{c[1]}x{c[2]}x{c[3]}-ld{c[4]}-{'forced' if c[5] else 'table'}")
 def test_bf16_output_matches_f32_then_convert(gpu, case):
     """out_dtype = TFORGE_BF16: the bf16 output equals tforge_convert_bf16 of the f32 output
