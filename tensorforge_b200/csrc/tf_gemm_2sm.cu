@@ -1,10 +1,10 @@
-// tf_gemm_2sm.cu -- fused GEMM on a CTA pair (tcgen05 cta_group::2), 256 x 256 output tiles.
+// tf_gemm_2sm.cu -- fused GEMM on a CTA pair (tcgen05 cta_group::2), 256 x 256 or 256 x 240 output tiles.
 //
 // Same operator and epilogue as tf_gemm_tc.cu (matmul, mbr = relu(A @ B + bias),
 // matmul_add), for large problems.  Two CTAs on two SMs form a cluster; CTA r of the pair
-// loads A rows [m0 + 128 r, +128) and B columns [n0 + 128 r, +128) into its own shared
-// memory (plain TMA tile loads, no multicast), and one pair MMA (M = 256, N = 256) reads
-// A from both CTAs and B from both halves, so each SM reads only half of B per FLOP.
+// loads A rows [m0 + 128 r, +128) and B columns [n0 + (BN / 2) r, +128) into its own shared
+// memory (plain TMA tile loads, no multicast), and one pair MMA (M = 256, N = BN) reads A
+// from both CTAs and B from both halves, so each SM reads only half of B per FLOP.
 //
 // fp32-accurate mode (3xTF32): per K step the MMA issues lo*hi, hi*lo and hi*hi.  The
 // split of A goes to tensor memory (tcgen05.st), so the MMAs read only B from shared
