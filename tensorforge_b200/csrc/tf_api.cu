@@ -56,8 +56,12 @@ EncodeTiledFn encode_fn() {
 // 2-D row-major tensor [rows x cols] with pitch `ld` elements; box = {box_cols, box_rows};
 // 128-byte swizzle (16-byte atoms, or 32-byte atoms with `atom32`, the layout the tensor
 // cores require for N-contiguous 32-bit operands); out-of-range elements read as zero.
+// Shared-memory layouts of a tile map: 128-B swizzle, its 32-B-atom form (MN-major TF32
+// operands), 64-B swizzle (bf16 output boxes), none (transposed output boxes).
+enum Swz { SW128 = 0, SW128_A32 = 1, SW64 = 2, SWNONE = 3 };
+
 int make_tmap(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols, int64_t ld,
-              uint32_t box_cols, uint32_t box_rows, bool atom32 = false, bool swizzle64 = false) {
+              uint32_t box_cols, uint32_t box_rows, int swz = SW128) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     g_last_error = "cuTensorMapEncodeTiled unavailable";
@@ -70,8 +74,10 @@ int make_tmap(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                    const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   swizzle64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                             : (atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B),
+                   swz == SW64        ? CU_TENSOR_MAP_SWIZZLE_64B
+                   : swz == SWNONE    ? CU_TENSOR_MAP_SWIZZLE_NONE
+                   : swz == SW128_A32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                      : CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -377,7 +383,7 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   CUtensorMap tmA, tmB;
   int rc = make_tmap(&tmA, A, bf16, a->M, a->K, lda, bk, 128);
   if (rc) return rc;
-  rc = make_tmap(&tmB, B, bf16, a->K, a->N, ldb, 128 / esz, bk, /*atom32=*/!bf16);
+  rc = make_tmap(&tmB, B, bf16, a->K, a->N, ldb, 128 / esz, bk, bf16 ? SW128 : SW128_A32);
   if (rc) return rc;
   TcParams p{};
   p.bias = a->bias;
@@ -396,6 +402,8 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
   cudaError_t e;
   const int splits = pair_splits(cfg, a->M, a->N, a->K);
+  // Pair kernels that accumulate the transposed tile store 32-row x 128-column boxes.
+  const bool swapped = cfg.pair && !cfg.persist && pair_transposed(cfg.prec, cfg.bn);
   if (cfg.pair && splits > 1) {
     // Split-K: raw partial sums of each k-range into slice z of a pooled workspace (rows
     // padded to whole tiles so no tile crosses a slice), then one pass sums the slices in
@@ -408,7 +416,8 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
     cudaError_t e2 = cudaMallocFromPoolAsync(&ws, sizeof(float) * (size_t)splits * mp * a->N, pool, st);
     if (e2 != cudaSuccess) return cuda_fail(e2, "cudaMallocFromPoolAsync(split-K workspace)");
     CUtensorMap tmW;
-    rc = make_tmap(&tmW, ws, false, splits * mp, a->N, a->N, 32, 128);
+    rc = swapped ? make_tmap(&tmW, ws, false, splits * mp, a->N, a->N, 128, 32, SWNONE)
+                 : make_tmap(&tmW, ws, false, splits * mp, a->N, a->N, 32, 128);
     if (rc) {
       cudaFreeAsync(ws, st);
       return rc;
@@ -422,16 +431,18 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
     cudaFreeAsync(ws, st);
   } else if (cfg.persist) {
     CUtensorMap tmO;
-    rc = make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, false, ob16);
+    rc = make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, ob16 ? SW64 : SW128);
     if (rc) return rc;
     e = launch_gemm_pair_persistent(cfg.prec, cfg.stages, epi, tmA, tmB, tmO, p, st);
   } else if (cfg.pair) {
     CUtensorMap tmO, tmC;
-    rc = make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, false, ob16);
+    rc = swapped ? make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 128, 32, SWNONE)
+                 : make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, ob16 ? SW64 : SW128);
     if (rc) return rc;
     tmC = tmO;
     if (a->workload == TFORGE_MATMUL_ADD) {
-      rc = make_tmap(&tmC, a->C_res, false, a->M, a->N, ldc, 32, 128);
+      rc = swapped ? make_tmap(&tmC, a->C_res, false, a->M, a->N, ldc, 128, 32, SWNONE)
+                   : make_tmap(&tmC, a->C_res, false, a->M, a->N, ldc, 32, 128);
       if (rc) return rc;
     }
     e = launch_gemm_pair(cfg.prec, cfg.stages, cfg.bn, epi, tmA, tmB, tmO, tmC, p, st);
@@ -457,7 +468,7 @@ bool select_tc_config(int mode, int64_t M, int64_t N, int64_t K, TcConfig *out) 
 
 int encode_operand_map(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t cols,
                        int64_t ld, uint32_t box_cols, uint32_t box_rows, bool atom32) {
-  return make_tmap(m, base, bf16, rows, cols, ld, box_cols, box_rows, atom32);
+  return make_tmap(m, base, bf16, rows, cols, ld, box_cols, box_rows, atom32 ? SW128_A32 : SW128);
 }
 
 void set_last_error(const char *msg) { g_last_error = msg; }

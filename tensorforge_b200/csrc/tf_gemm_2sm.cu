@@ -38,6 +38,14 @@
 // Tile width BN: 256, or 240 when that needs no more waves of SM pairs (each CTA's MMA
 // half is then the first 120 of the 128 B columns it loads).
 //
+// TF32 with 256-wide tiles (kTf32Swap) exchanges the MMA's operands: B's tile (MN-major,
+// which for 32-bit elements the tensor core reads through the 128B_BASE32B swizzle) is the M
+// side, local to each CTA, and A's tile the N side shared by the pair, so CTA r accumulates
+// the transposed tile: TMEM lane = output column n0 + 128 r + lane, TMEM column j = output
+// row (pair's first row) + j.  The loads are unchanged; the epilogue stores 32-row x
+// 128-column boxes.  (Measured on cuBLAS as well: its TF32 GEMM with the MN-major operand on
+// the N side ran 690 TFLOP/s at 8192^3 against 808 with it on the M side.)
+//
 // TF32 / BF16 modes have no converters: each CTA's TMA (.cta_group::2 form) completes on
 // the LEADER's full[s], which expects both CTAs' bytes, and the MMA reads A and B from
 // shared memory.
@@ -66,6 +74,11 @@ constexpr bool kPairHiDirect = kPairSplit == 1;
 
 // bf16-output epilogue staging box: 128 rows x 32 bf16 columns.
 constexpr int kEpiBoxBytesB = 128 * 64;
+
+#ifndef TF_TF32_SWAP
+#define TF_TF32_SWAP 1
+#endif
+constexpr bool kTf32Swap = TF_TF32_SWAP;
 
 template <int PREC, int STAGES>
 struct PairLayout {
@@ -174,7 +187,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   using L = PairLayout<PREC, STAGES>;
   constexpr bool kX3 = PREC == PREC_X3;
   constexpr bool kTF32 = PREC != PREC_BF16;
-  constexpr uint32_t kIdesc = instr_desc(kTF32 ? 2u : 1u, 256, BN);
+  // TF32, 256-wide tiles: operands exchanged (B's tile on the M side), transposed epilogue.
+  constexpr bool kSwap = PREC == PREC_TF32 && BN == 256 && kTf32Swap;
+  constexpr uint32_t kIdesc = kSwap ? instr_desc_a_mn(2u, 256, 256) : instr_desc(kTF32 ? 2u : 1u, 256, BN);
   // BN = 240: each CTA's MMA half is 120 B columns (the first 120 of the 128 it loads), and
   // the accumulator's last 32-column chunk holds only 16 output columns.
   static_assert(BN == 256 || BN == 240, "pair tile width");
@@ -340,7 +355,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
             const uint64_t ad = smem_desc(sbase + L::a_off(s) + ks * 32, 16, 1024, 2);
             const uint64_t bd = smem_desc(sbase + L::b_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
                                           L::kBSbo, L::kBSwz);
-            mma_ss_pair<kTF32>(tmem, ad, bd, kIdesc, accum);
+            if constexpr (kSwap)
+              mma_ss_pair<kTF32>(tmem, bd, ad, kIdesc, accum);
+            else
+              mma_ss_pair<kTF32>(tmem, ad, bd, kIdesc, accum);
           }
           accum = 1u;
         }
@@ -450,7 +468,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
     if (warp == 4 && lane == 0)
       *epi_ok = (mbar_wait_cluster(accf, 0, wc, 128) && (EPI != EPI_MBR || mbar_wait(biasf, 0, wc))) ? 1u : 0u;
     named_barrier(9, kEpiThreads);
-    if (*epi_ok) {
+    if (kSwap && *epi_ok) {
+      // Transposed accumulator: thread (q, lane) holds output column nb + r for the 256 rows
+      // mp0 .. mp0 + 255, 32 per chunk c; chunk c goes through box c (32 rows x 128 columns,
+      // row-major, no swizzle: a warp writes 128 consecutive bytes per row) and one TMA store.
+      tc_fence_after();
+      const int q = warp & 3, r = q * 32 + lane;
+      const int mp0 = m0 - (int)rank * 128, nb = n0 + (int)rank * 128;
+      const bool cta_cols = nb < p.N;
+      const int split_off = (int)blockIdx.z * p.split_rows;
+      const float *bias_f = reinterpret_cast<const float *>(bias_s);
+      const float bcol = EPI == EPI_MBR ? bias_f[(int)rank * 128 + r] : 0.f;  // 0 beyond N
+      bool res_ok = true;
+      if constexpr (EPI == EPI_ADD) {
+        if (warp == 4 && lane == 0 && cta_cols) {
+          mbar_arrive_expect_tx(resf, 8 * L::kEpiBoxBytes);
+#pragma unroll 1
+          for (int c = 0; c < 8; ++c) tma_load_2d(sbase + c * L::kEpiBoxBytes, &tmC, nb, mp0 + 32 * c, resf);
+        }
+        res_ok = !cta_cols || mbar_wait_cluster(resf, 0, wc);
+      }
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t rr[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, rr);
+        tmem_ld_wait();
+        const int row0 = mp0 + 32 * c;
+        float *box = reinterpret_cast<float *>(smem + c * L::kEpiBoxBytes);
+        const bool live = res_ok && cta_cols && row0 < p.M;
+        if (live) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float v = __uint_as_float(rr[i]);
+            if constexpr (EPI == EPI_MBR) v = relu_ieee(__fadd_rn(v, bcol));
+            else if constexpr (EPI == EPI_ADD) v = __fadd_rn(v, box[i * 128 + r]);
+            box[i * 128 + r] = v;
+          }
+        }
+        fence_proxy_async_smem();
+        named_barrier(1 + c, 128);
+        if (q == 0 && lane == 0 && live) {
+          tma_store_2d(&tmO, sbase + c * L::kEpiBoxBytes, nb, row0 + split_off);
+          bulk_commit_group();
+        }
+      }
+      if (q == 0 && lane == 0) bulk_wait_group_read0();  // staging stays valid until read
+    } else if (*epi_ok) {
       tc_fence_after();
       constexpr int kChunksPerWarp = 8 / (L::kEpiWarps / 4);  // column chunks of 32 per warp
       const int q = warp & 3;
@@ -634,6 +697,8 @@ int pair_smem_bytes(int prec, int stages) {
 }
 
 int pair_tmem_cols(int prec) { return prec == PREC_X3 ? 512 : 256; }
+
+bool pair_transposed(int prec, int bn) { return prec == PREC_TF32 && bn == 256 && kTf32Swap; }
 
 cudaError_t launch_gemm_pair(int prec, int stages, int bn, int epi, const CUtensorMap &tmA,
                              const CUtensorMap &tmB, const CUtensorMap &tmO, const CUtensorMap &tmC,

@@ -78,6 +78,9 @@ cudaError_t simt_func_attributes(int epi, cudaFuncAttributes *attr, int *blocks_
 // clusters of two CTAs.
 int pair_smem_bytes(int prec, int stages);
 int pair_tmem_cols(int prec);
+// True when the pair kernel for (prec, bn) accumulates the transposed tile (TF32, 256 wide):
+// its output / C_res maps then use 32-row x 128-column boxes without swizzle.
+bool pair_transposed(int prec, int bn);
 // tmO / tmC: f32 maps of the output and of C_res (box 32 columns x 128 rows, 128-B
 // swizzle) for the TMA-store epilogue; tmC is read only by matmul_add.  bn 240 takes no
 // split-K (p.splits <= 1).

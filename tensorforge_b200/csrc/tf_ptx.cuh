@@ -378,6 +378,11 @@ __host__ __device__ constexpr uint32_t instr_desc(uint32_t fmt, uint32_t m, uint
   return (1u << 4) | (fmt << 7) | (fmt << 10) | (0u << 15) | (1u << 16) | ((n >> 3) << 17) |
          ((m >> 4) << 24);
 }
+// The same with the majors exchanged: A MN-major (bit 15 = 1), B K-major (bit 16 = 0).
+__host__ __device__ constexpr uint32_t instr_desc_a_mn(uint32_t fmt, uint32_t m, uint32_t n) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 15) | (0u << 16) | ((n >> 3) << 17) |
+         ((m >> 4) << 24);
+}
 
 // Two f32 values rounded to nearest-even bf16, packed: lo in bits [0, 16), hi in [16, 32).
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
