@@ -492,7 +492,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       for (int c = 0; c < 8; ++c) {
         uint32_t rr[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, rr);
-        tmem_ld_wait();
+        tmem_ld_wait(rr);
         const int row0 = mp0 + 32 * c;
         float *box = reinterpret_cast<float *>(smem + c * L::kEpiBoxBytes);
         const bool live = res_ok && cta_cols && row0 < p.M;
@@ -534,7 +534,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       for (int c = c0; c < c0 + kChunksPerWarp; ++c) {
         uint32_t rr[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, rr);
-        tmem_ld_wait();
+        tmem_ld_wait(rr);
         const int col0 = n0 + c * 32;
         uint8_t *box = smem + c * L::kEpiBoxBytes + r * 128;
         // Epilogue of columns col0 + 4 j .. + 3 (matmul_add: the residual sits in the box).

@@ -242,7 +242,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           for (int j = 0; j < 8; ++j)
             cr[j] = row_ok && col0 + 4 * j < p.N ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        tmem_ld_wait();
+        tmem_ld_wait(rr);
         uint8_t *box = boxes + (c & 1) * L::kBoxBytes;
         if (et == 0) bulk_wait_group_read1();
         named_barrier(2, 128);

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_acc + ((uint32_t)(q * 32) << 16) + c * 32, r);
-        tmem_ld_wait();
+        tmem_ld_wait(r);
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < p.N) {
 #pragma unroll
