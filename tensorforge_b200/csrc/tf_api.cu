@@ -553,19 +553,15 @@ int tforge_gemm(const tforge_gemm_args *a, void *stream) {
     uint16_t *sa = static_cast<uint16_t *>(scratch);
     uint16_t *sb = reinterpret_cast<uint16_t *>(static_cast<char *>(scratch) + ((abytes + 255) & ~size_t(255)));
     if (abytes) {
-      // Packed copy of a possibly pitched A: convert row blocks when pitched.
-      if (lda == a->K) e = launch_convert_bf16(static_cast<const float *>(a->A), sa, a->M * a->K, st);
-      else
-        for (int64_t r = 0; r < a->M && e == cudaSuccess; ++r)
-          e = launch_convert_bf16(static_cast<const float *>(a->A) + r * lda, sa + r * a->K, a->K, st);
+      // Packed bf16 copy of a possibly pitched A (one launch either way).
+      e = lda == a->K ? launch_convert_bf16(static_cast<const float *>(a->A), sa, a->M * a->K, st)
+                      : launch_convert_rows_bf16(static_cast<const float *>(a->A), lda, sa, a->K, a->M, a->K, st);
       A = sa;
       la = a->K;
     }
     if (bbytes && e == cudaSuccess) {
-      if (ldb == a->N) e = launch_convert_bf16(static_cast<const float *>(a->B), sb, a->K * a->N, st);
-      else
-        for (int64_t r = 0; r < a->K && e == cudaSuccess; ++r)
-          e = launch_convert_bf16(static_cast<const float *>(a->B) + r * ldb, sb + r * a->N, a->N, st);
+      e = ldb == a->N ? launch_convert_bf16(static_cast<const float *>(a->B), sb, a->K * a->N, st)
+                      : launch_convert_rows_bf16(static_cast<const float *>(a->B), ldb, sb, a->N, a->K, a->N, st);
       B = sb;
       lb = a->N;
     }

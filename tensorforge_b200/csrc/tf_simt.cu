@@ -196,6 +196,31 @@ __global__ void convert_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *
     y[i] = __float2bfloat16_rn(x[i]);
 }
 
+// Eight elements per step (x and y 16-byte aligned): two 16-byte loads, one 16-byte store;
+// the same round-to-nearest-even per element as __float2bfloat16_rn.
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+__device__ __forceinline__ uint4 bf16x8(const float4 a, const float4 b) {
+  return make_uint4(bf16x2_bits(a.x, a.y), bf16x2_bits(a.z, a.w), bf16x2_bits(b.x, b.y), bf16x2_bits(b.z, b.w));
+}
+__global__ void convert_bf16_vec8_kernel(const float4 *__restrict__ x, uint4 *__restrict__ y, int64_t n8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = bf16x8(__ldg(x + 2 * i), __ldg(x + 2 * i + 1));
+}
+
+// Pitched rows, eight elements per step (N, both pitches multiples of 8, bases aligned).
+__global__ void convert_rows_bf16_vec8_kernel(const float *__restrict__ x, int64_t lds, uint16_t *__restrict__ y,
+                                              int64_t ldd, int64_t M, int64_t n8) {
+  const int64_t total = M * n8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / n8, c = (i - r * n8) * 8;
+    const float4 *src = reinterpret_cast<const float4 *>(x + r * lds + c);
+    *reinterpret_cast<uint4 *>(y + r * ldd + c) = bf16x8(__ldg(src), __ldg(src + 1));
+  }
+}
+
 // Pitched f32 -> bf16 rows (one element per thread step; the general bf16-output path).
 __global__ void convert_rows_bf16_kernel(const float *__restrict__ x, int64_t lds, __nv_bfloat16 *__restrict__ y,
                                          int64_t ldd, int64_t M, int64_t N) {
@@ -299,13 +324,26 @@ cudaError_t launch_elementwise(int op, const float *X, const float *Y, float *Z,
 cudaError_t launch_convert_rows_bf16(const float *src, int64_t lds, uint16_t *dst, int64_t ldd, int64_t M,
                                      int64_t N, cudaStream_t stream) {
   if (M == 0 || N == 0) return cudaSuccess;
-  convert_rows_bf16_kernel<<<grid_for(M * N, 256), 256, 0, stream>>>(src, lds, reinterpret_cast<__nv_bfloat16 *>(dst),
-                                                                     ldd, M, N);
+  const bool vec = N % 8 == 0 && lds % 8 == 0 && ldd % 8 == 0 && ((uintptr_t)src % 16) == 0 && ((uintptr_t)dst % 16) == 0;
+  if (vec)
+    convert_rows_bf16_vec8_kernel<<<grid_for(M * N / 8, 256), 256, 0, stream>>>(src, lds, dst, ldd, M, N / 8);
+  else
+    convert_rows_bf16_kernel<<<grid_for(M * N, 256), 256, 0, stream>>>(src, lds, reinterpret_cast<__nv_bfloat16 *>(dst),
+                                                                       ldd, M, N);
   return cudaGetLastError();
 }
 
 cudaError_t launch_convert_bf16(const float *x, uint16_t *y, int64_t n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
+  if (((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0 && n >= 8) {
+    // Aligned bulk in 8-element steps, the remaining n % 8 elements one by one.
+    const int64_t n8 = n / 8;
+    convert_bf16_vec8_kernel<<<grid_for(n8, 256), 256, 0, stream>>>(reinterpret_cast<const float4 *>(x),
+                                                                    reinterpret_cast<uint4 *>(y), n8);
+    if (n % 8)
+      convert_bf16_kernel<<<1, 32, 0, stream>>>(x + n8 * 8, reinterpret_cast<__nv_bfloat16 *>(y) + n8 * 8, n % 8);
+    return cudaGetLastError();
+  }
   convert_bf16_kernel<<<grid_for(n, 256), 256, 0, stream>>>(
       x, reinterpret_cast<__nv_bfloat16 *>(y), n);
   return cudaGetLastError();

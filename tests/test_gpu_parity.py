@@ -539,6 +539,38 @@ def test_bf16_output_matches_f32_then_convert(gpu, case):
     assert bool(torch.isnan(out16[0, :n].float()).all())
 
 
+def _bf16_rne_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16 bit patterns (NaNs left to the caller)."""
+    u = x.view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("n,xoff,yoff", [(1, 0, 0), (7, 0, 0), (8, 0, 0), (1000003, 0, 0), (4099, 1, 0),
+                                         (4099, 0, 3), (65536, 4, 8)])
+def test_convert_bf16_rounds_to_nearest_even(gpu, n, xoff, yoff):
+    """tforge_convert_bf16: 8-element vector steps when both ends are 16-byte aligned, the
+    scalar kernel for the n % 8 tail and for misaligned buffers; every element rounded to
+    nearest even (ties, subnormals, infinities; NaN stays NaN)."""
+    import torch
+
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal(n) * np.float32(2.0) ** rng.integers(-130, 120, n)).astype(np.float32)
+    special = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1.0 + 2.0 ** -8, 1.0 + 3 * 2.0 ** -8, 1e-45,
+                        -3.4e38, 1.17e-38], np.float32)
+    x[: min(n, special.size)] = special[: min(n, special.size)]
+    dev = torch.device("cuda", 0)
+    xb = torch.zeros(n + 8, device=dev)
+    xb[xoff:xoff + n] = torch.from_numpy(x).to(dev)
+    yb = torch.zeros(n + 8, device=dev, dtype=torch.int16)
+    _lib.check(_lib.lib().tforge_convert_bf16(xb.data_ptr() + 4 * xoff, yb.data_ptr() + 2 * yoff, n, None), "convert")
+    torch.cuda.synchronize()
+    got = yb[yoff:yoff + n].cpu().numpy().view(np.uint16)
+    nan = np.isnan(x)
+    assert np.array_equal(got[~nan], _bf16_rne_bits(x)[~nan])
+    assert bool(np.all((got[nan] & 0x7F80) == 0x7F80) and np.all(got[nan] & 0x7F))
+    assert bool((yb[:yoff] == 0).all()) and bool((yb[yoff + n:] == 0).all())  # nothing outside
+
+
 def test_concurrent_streams_match_single_stream(gpu):
     """Calls interleaved on two streams (split-K workspace and bf16 scratch come from the
     stream-ordered pool) give the same bits as the same calls on one stream."""
