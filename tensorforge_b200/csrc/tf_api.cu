@@ -552,14 +552,22 @@ int tforge_gemm(const tforge_gemm_args *a, void *stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocFromPoolAsync(bf16 scratch)");
     uint16_t *sa = static_cast<uint16_t *>(scratch);
     uint16_t *sb = reinterpret_cast<uint16_t *>(static_cast<char *>(scratch) + ((abytes + 255) & ~size_t(255)));
-    if (abytes) {
+    if (abytes && bbytes && lda == a->K && ldb == a->N) {
+      // Both operands packed: one launch converts both.
+      e = launch_convert_bf16_two(static_cast<const float *>(a->A), sa, a->M * a->K, static_cast<const float *>(a->B), sb,
+                                  a->K * a->N, st);
+      A = sa;
+      la = a->K;
+      B = sb;
+      lb = a->N;
+    } else if (abytes) {
       // Packed bf16 copy of a possibly pitched A (one launch either way).
       e = lda == a->K ? launch_convert_bf16(static_cast<const float *>(a->A), sa, a->M * a->K, st)
                       : launch_convert_rows_bf16(static_cast<const float *>(a->A), lda, sa, a->K, a->M, a->K, st);
       A = sa;
       la = a->K;
     }
-    if (bbytes && e == cudaSuccess) {
+    if (bbytes && B != sb && e == cudaSuccess) {
       e = ldb == a->N ? launch_convert_bf16(static_cast<const float *>(a->B), sb, a->K * a->N, st)
                       : launch_convert_rows_bf16(static_cast<const float *>(a->B), ldb, sb, a->N, a->K, a->N, st);
       B = sb;

@@ -126,6 +126,9 @@ int simt_tile_size(int64_t M, int64_t N);  // 128 or 64 (square tiles)
 cudaError_t launch_elementwise(int op, const float *X, const float *Y, float *Z, int64_t M,
                                int64_t N, cudaStream_t stream);
 cudaError_t launch_convert_bf16(const float *x, uint16_t *y, int64_t n, cudaStream_t stream);
+// Both conversions in one launch when both arrays are 16-byte aligned multiples of 8 elements.
+cudaError_t launch_convert_bf16_two(const float *x1, uint16_t *y1, int64_t n1, const float *x2, uint16_t *y2,
+                                    int64_t n2, cudaStream_t stream);
 // Split-K epilogue: out[m, n] = epi(sum over s = 0..S-1, in order, of ws[s * slice + m * N + n]);
 // N a multiple of 4, 16-byte-aligned rows.
 cudaError_t launch_splitk_reduce(int epi, const float *ws, int splits, int64_t slice, int64_t M, int64_t N,

@@ -210,6 +210,19 @@ __global__ void convert_bf16_vec8_kernel(const float4 *__restrict__ x, uint4 *__
     y[i] = bf16x8(__ldg(x + 2 * i), __ldg(x + 2 * i + 1));
 }
 
+// Two packed arrays in one launch (A and B of a BF16-mode call), eight elements per step.
+__global__ void convert_bf16_two_vec8_kernel(const float4 *__restrict__ x1, uint4 *__restrict__ y1, int64_t n1_8,
+                                             const float4 *__restrict__ x2, uint4 *__restrict__ y2, int64_t n2_8) {
+  const int64_t total = n1_8 + n2_8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < n1_8) y1[i] = bf16x8(__ldg(x1 + 2 * i), __ldg(x1 + 2 * i + 1));
+    else {
+      const int64_t j = i - n1_8;
+      y2[j] = bf16x8(__ldg(x2 + 2 * j), __ldg(x2 + 2 * j + 1));
+    }
+  }
+}
+
 // Pitched rows, eight elements per step (N, both pitches multiples of 8, bases aligned).
 __global__ void convert_rows_bf16_vec8_kernel(const float *__restrict__ x, int64_t lds, uint16_t *__restrict__ y,
                                               int64_t ldd, int64_t M, int64_t n8) {
@@ -330,6 +343,20 @@ cudaError_t launch_convert_rows_bf16(const float *src, int64_t lds, uint16_t *ds
   else
     convert_rows_bf16_kernel<<<grid_for(M * N, 256), 256, 0, stream>>>(src, lds, reinterpret_cast<__nv_bfloat16 *>(dst),
                                                                        ldd, M, N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_convert_bf16_two(const float *x1, uint16_t *y1, int64_t n1, const float *x2, uint16_t *y2,
+                                    int64_t n2, cudaStream_t stream) {
+  const bool vec = n1 % 8 == 0 && n2 % 8 == 0 && ((uintptr_t)x1 % 16) == 0 && ((uintptr_t)y1 % 16) == 0 &&
+                   ((uintptr_t)x2 % 16) == 0 && ((uintptr_t)y2 % 16) == 0;
+  if (!vec || n1 + n2 == 0) {
+    cudaError_t e = launch_convert_bf16(x1, y1, n1, stream);
+    return e == cudaSuccess ? launch_convert_bf16(x2, y2, n2, stream) : e;
+  }
+  convert_bf16_two_vec8_kernel<<<grid_for((n1 + n2) / 8, 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4 *>(x1), reinterpret_cast<uint4 *>(y1), n1 / 8, reinterpret_cast<const float4 *>(x2),
+      reinterpret_cast<uint4 *>(y2), n2 / 8);
   return cudaGetLastError();
 }
 
