@@ -47,7 +47,7 @@ class Launch(C.Structure):
 
 class Config(C.Structure):
     _fields_ = [("kernel", C.c_int32), ("bn", C.c_int32), ("stages", C.c_int32),
-                ("persistent", C.c_int32), ("split_k", C.c_int32)]
+                ("persistent", C.c_int32), ("split_k", C.c_int32), ("b_layout", C.c_int32)]
 
 
 # Every symbol include/tforge.h declares, with its ctypes signature.
@@ -121,13 +121,15 @@ def describe(workload: str, m: int, n: int, k: int, mode: str = "fp32") -> dict:
     return out.as_dict()
 
 
-def set_config(kernel: int = 0, bn: int = 0, stages: int = 0, persistent: int = 0, split_k: int = 0) -> None:
+def set_config(kernel: int = 0, bn: int = 0, stages: int = 0, persistent: int = 0, split_k: int = 0,
+               b_layout: int = 0) -> None:
     """Force a kernel configuration (kernel 1 = one-CTA tcgen05, 2 = SIMT, 3 = CTA pair;
-    split_k: pairs per tile for the pair kernel, 1 = none); all zeros = table."""
-    if kernel == 0 and bn == 0 and stages == 0 and persistent == 0 and split_k == 0:
+    split_k: pairs per tile for the pair kernel, 1 = none; b_layout (TF32 pair kernels):
+    1 = B as given, 2 = a transposed K-major copy); all zeros = table."""
+    if kernel == 0 and bn == 0 and stages == 0 and persistent == 0 and split_k == 0 and b_layout == 0:
         check(lib().tforge_set_config(None), "tforge_set_config")
         return
-    cfg = Config(kernel, bn, stages, persistent, split_k)
+    cfg = Config(kernel, bn, stages, persistent, split_k, b_layout)
     check(lib().tforge_set_config(C.byref(cfg)), "tforge_set_config")
 
 

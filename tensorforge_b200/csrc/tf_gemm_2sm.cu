@@ -179,7 +179,7 @@ __device__ __forceinline__ void relay_stages(uint32_t conv0, uint32_t ready0, ui
   }
 }
 
-template <int PREC, int STAGES, int EPI, int SPLIT, int BN, bool OUTB>
+template <int PREC, int STAGES, int EPI, int SPLIT, int BN, bool OUTB, bool BKM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STAGES>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmC,
@@ -187,9 +187,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   using L = PairLayout<PREC, STAGES>;
   constexpr bool kX3 = PREC == PREC_X3;
   constexpr bool kTF32 = PREC != PREC_BF16;
-  // TF32, 256-wide tiles: operands exchanged (B's tile on the M side), transposed epilogue.
-  constexpr bool kSwap = PREC == PREC_TF32 && BN == 256 && kTf32Swap;
-  constexpr uint32_t kIdesc = kSwap ? instr_desc_a_mn(2u, 256, 256) : instr_desc(kTF32 ? 2u : 1u, 256, BN);
+  // BKM (TF32, 256-wide tiles): B is a transposed copy, loaded and read K-major like A.
+  static_assert(!BKM || (PREC == PREC_TF32 && BN == 256 && !OUTB), "K-major B configuration");
+  // TF32, 256-wide tiles, B as given: operands exchanged (B's MN-major tile on the M side),
+  // transposed epilogue.
+  constexpr bool kSwap = PREC == PREC_TF32 && BN == 256 && kTf32Swap && !BKM;
+  constexpr uint32_t kIdesc = kSwap  ? instr_desc_a_mn(2u, 256, 256)
+                              : BKM ? (instr_desc(2u, 256, 256) & ~(1u << 16))  // B K-major
+                                    : instr_desc(kTF32 ? 2u : 1u, 256, BN);
   // BN = 240: each CTA's MMA half is 120 B columns (the first 120 of the 128 it loads), and
   // the accumulator's last 32-column chunk holds only 16 output columns.
   static_assert(BN == 256 || BN == 240, "pair tile width");
@@ -305,10 +310,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       } else {
         if (rank == 0) mbar_arrive_expect_tx(full0 + 8 * s, 2 * L::kStageBytes);
         tma_load_2d_pair(sbase + L::a_off(s), &tmA, kc, m0, lead_full0 + 8 * s);
+        if constexpr (BKM) {
+          tma_load_2d_pair(sbase + L::b_off(s), &tmB, kc, nb, lead_full0 + 8 * s);  // 128 n-rows x 32 k
+        } else {
 #pragma unroll
-        for (int j = 0; j < L::kBBlocks; ++j)
-          tma_load_2d_pair(sbase + L::b_off(s) + j * (L::kBK * 128), &tmB, nb + j * L::kNBlk, kc,
-                           lead_full0 + 8 * s);
+          for (int j = 0; j < L::kBBlocks; ++j)
+            tma_load_2d_pair(sbase + L::b_off(s) + j * (L::kBK * 128), &tmB, nb + j * L::kNBlk, kc,
+                             lead_full0 + 8 * s);
+        }
       }
     }
     if (*abort_flag) {
@@ -353,8 +362,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
             mma_ts_pair_tf32(tmem, a_hi, bh, kIdesc, 1u);
           } else {
             const uint64_t ad = smem_desc(sbase + L::a_off(s) + ks * 32, 16, 1024, 2);
-            const uint64_t bd = smem_desc(sbase + L::b_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
-                                          L::kBSbo, L::kBSwz);
+            const uint64_t bd = BKM ? smem_desc(sbase + L::b_off(s) + ks * 32, 16, 1024, 2)
+                                    : smem_desc(sbase + L::b_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
+                                                L::kBSbo, L::kBSwz);
             if constexpr (kSwap)
               mma_ss_pair<kTF32>(tmem, bd, ad, kIdesc, accum);
             else
@@ -626,11 +636,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   }
 }
 
-template <int PREC, int STAGES, int EPI, int BN, bool OUTB>
+template <int PREC, int STAGES, int EPI, int BN, bool OUTB, bool BKM = false>
 cudaError_t launch_pair_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
                              const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   using L = PairLayout<PREC, STAGES>;
-  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit, BN, OUTB>;
+  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit, BN, OUTB, BKM>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -650,6 +660,12 @@ cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, cons
                             const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   // The 240-wide tile stores its last 16 columns through p.out, so it takes no split-K.
   if (BN != 256 && p.splits > 1) return cudaErrorInvalidValue;
+  if (p.b_kmajor) {
+    if constexpr (PREC == PREC_TF32 && BN == 256)
+      return p.out_bf16 ? cudaErrorInvalidValue
+                        : launch_pair_kern<PREC, STAGES, EPI, BN, false, true>(tmA, tmB, tmO, tmC, p, stream);
+    return cudaErrorInvalidValue;
+  }
   if (p.out_bf16) {
     if constexpr (PREC == PREC_BF16 && EPI == EPI_MBR && BN == 256)
       return p.splits > 1 ? cudaErrorInvalidValue
@@ -673,9 +689,9 @@ cudaError_t launch_pair_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &
 template <int PREC, int STAGES, int BN>
 cudaError_t pair_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
   using L = PairLayout<PREC, STAGES>;
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit, BN, false>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit, BN, false>)
-                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit, BN, false>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit, BN, false, false>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit, BN, false, false>)
+                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit, BN, false, false>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);

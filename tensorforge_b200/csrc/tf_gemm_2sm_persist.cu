@@ -64,15 +64,17 @@ __device__ __forceinline__ void pause_ns(uint64_t ns) {
   while (globaltimer() - t0 < ns) __nanosleep(1000);
 }
 
-template <int PREC, int STAGES, int EPI, bool OUTB>
+template <int PREC, int STAGES, int EPI, bool OUTB, bool BKM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 const __grid_constant__ CUtensorMap tmO, const TcParams p) {
   using L = PersistLayout<PREC, STAGES>;
   constexpr bool kTF32 = PREC == PREC_TF32;
-  constexpr uint32_t kIdesc = instr_desc(kTF32 ? 2u : 1u, 256, 256);
+  // BKM (TF32): B is a transposed copy, loaded and read K-major like A.
+  constexpr uint32_t kIdesc = BKM ? (instr_desc(2u, 256, 256) & ~(1u << 16)) : instr_desc(kTF32 ? 2u : 1u, 256, 256);
   // bf16 output (OUTB): BF16 precision and the mbr epilogue only.
   static_assert(!OUTB || (PREC == PREC_BF16 && EPI == EPI_MBR), "bf16 output configuration");
+  static_assert(!BKM || PREC == PREC_TF32, "K-major B configuration");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -147,9 +149,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const uint32_t slot = sbase + s * L::kStageBytes;
         if (rank == 0) mbar_arrive_expect_tx(full0 + 8 * s, 2 * L::kStageBytes);
         tma_load_2d_pair(slot, &tmA, kc, m0, lead_full0 + 8 * s);
+        if constexpr (BKM) {
+          tma_load_2d_pair(slot + L::kABytes, &tmB, kc, nb, lead_full0 + 8 * s);  // 128 n-rows x 32 k
+        } else {
 #pragma unroll
-        for (int j = 0; j < L::kBBlocks; ++j)
-          tma_load_2d_pair(slot + L::kABytes + j * (L::kBK * 128), &tmB, nb + j * L::kNBlk, kc, lead_full0 + 8 * s);
+          for (int j = 0; j < L::kBBlocks; ++j)
+            tma_load_2d_pair(slot + L::kABytes + j * (L::kBK * 128), &tmB, nb + j * L::kNBlk, kc, lead_full0 + 8 * s);
+        }
       }
     }
     if (*abort_flag) {
@@ -186,7 +192,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 #pragma unroll
         for (int ks = 0; ks < L::kKSteps; ++ks) {
           const uint64_t ad = smem_desc(slot + ks * 32, 16, 1024, 2);
-          const uint64_t bd = smem_desc(slot + L::kABytes + ks * L::kUmmaK * 128, L::kBK * 128, L::kBSbo, L::kBSwz);
+          const uint64_t bd = BKM ? smem_desc(slot + L::kABytes + ks * 32, 16, 1024, 2)
+                                  : smem_desc(slot + L::kABytes + ks * L::kUmmaK * 128, L::kBK * 128, L::kBSbo, L::kBSwz);
           mma_ss_pair<kTF32>(acc, ad, bd, kIdesc, (kb | ks) ? 1u : 0u);
         }
         mma_commit_pair(empty0 + 8 * s, 0x3);
@@ -309,10 +316,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 }
 
 // Co-resident clusters of one instantiation on the current device (0 on failure).
-template <int PREC, int STAGES, int EPI, bool OUTB = false>
+template <int PREC, int STAGES, int EPI, bool OUTB = false, bool BKM = false>
 int persist_clusters() {
   using L = PersistLayout<PREC, STAGES>;
-  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB>;
+  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM>;
   static int cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -347,16 +354,16 @@ int persist_clusters() {
   return n;
 }
 
-template <int PREC, int STAGES, int EPI, bool OUTB>
+template <int PREC, int STAGES, int EPI, bool OUTB, bool BKM = false>
 cudaError_t launch_persist_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
                                 const TcParams &p, cudaStream_t stream) {
   using L = PersistLayout<PREC, STAGES>;
-  const int clusters = persist_clusters<PREC, STAGES, EPI, OUTB>();
+  const int clusters = persist_clusters<PREC, STAGES, EPI, OUTB, BKM>();
   if (clusters <= 0) return cudaErrorInvalidConfiguration;
   const int64_t tiles = (int64_t)((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int pairs = tiles < clusters ? (int)tiles : clusters;
-  gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB><<<2 * pairs, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB,
-                                                                                                       tmO, p);
+  gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM><<<2 * pairs, L::kThreads, L::kSmemBytes, stream>>>(
+      tmA, tmB, tmO, p);
   return cudaGetLastError();
 }
 
@@ -364,6 +371,11 @@ template <int PREC, int STAGES, int EPI>
 cudaError_t launch_persist_one(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
                                const TcParams &p, cudaStream_t stream) {
   if (p.splits > 1) return cudaErrorInvalidValue;
+  if (p.b_kmajor) {
+    if constexpr (PREC == PREC_TF32)
+      return p.out_bf16 ? cudaErrorInvalidValue : launch_persist_kern<PREC, STAGES, EPI, false, true>(tmA, tmB, tmO, p, stream);
+    return cudaErrorInvalidValue;
+  }
   if (p.out_bf16) {
     if constexpr (PREC == PREC_BF16 && EPI == EPI_MBR)
       return launch_persist_kern<PREC, STAGES, EPI, true>(tmA, tmB, tmO, p, stream);
@@ -386,9 +398,9 @@ cudaError_t launch_persist_epi(int epi, const CUtensorMap &tmA, const CUtensorMa
 template <int PREC, int STAGES>
 cudaError_t persist_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
   using L = PersistLayout<PREC, STAGES>;
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MBR, false>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_ADD, false>)
-                                   : reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MATMUL, false>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MBR, false, false>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_ADD, false, false>)
+                                   : reinterpret_cast<const void *>(gemm_pair_persistent_kernel<PREC, STAGES, EPI_MATMUL, false, false>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);

@@ -50,6 +50,9 @@ struct TcParams {
   // rows, 64-B swizzle).  BF16 precision, mbr epilogue, 256-wide pair tiles or the
   // persistent pair kernel only.
   int32_t out_bf16;
+  // 1 (TF32, 256-wide pair tiles or the persistent pair kernel): tmB maps a transposed copy
+  // of B (N x K, K-major tiles of 128 columns x 32 k); the MMAs read both operands K-major.
+  int32_t b_kmajor;
 };
 
 struct TcConfig {
@@ -126,6 +129,9 @@ int simt_tile_size(int64_t M, int64_t N);  // 128 or 64 (square tiles)
 cudaError_t launch_elementwise(int op, const float *X, const float *Y, float *Z, int64_t M,
                                int64_t N, cudaStream_t stream);
 cudaError_t launch_convert_bf16(const float *x, uint16_t *y, int64_t n, cudaStream_t stream);
+// dst (cols x rows, pitch ldd) = transpose of src (rows x cols, pitch lds); rows < 2^21.
+cudaError_t launch_transpose_f32(const float *src, int64_t lds, float *dst, int64_t ldd, int64_t rows, int64_t cols,
+                                 cudaStream_t stream);
 // Both conversions in one launch when both arrays are 16-byte aligned multiples of 8 elements.
 cudaError_t launch_convert_bf16_two(const float *x1, uint16_t *y1, int64_t n1, const float *x2, uint16_t *y2,
                                     int64_t n2, cudaStream_t stream);

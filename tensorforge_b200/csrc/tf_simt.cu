@@ -210,6 +210,25 @@ __global__ void convert_bf16_vec8_kernel(const float4 *__restrict__ x, uint4 *__
     y[i] = bf16x8(__ldg(x + 2 * i), __ldg(x + 2 * i + 1));
 }
 
+// dst[c * ldd + r] = src[r * lds + c]: 32 x 32 tiles through shared memory (padded against
+// bank conflicts), coalesced reads along c and writes along r; 32 x 8 threads, 4 rows each.
+__global__ void transpose_f32_kernel(const float *__restrict__ src, int64_t lds, float *__restrict__ dst, int64_t ldd,
+                                     int64_t rows, int64_t cols) {
+  __shared__ float t[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int64_t r = r0 + threadIdx.y + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) t[threadIdx.y + i][threadIdx.x] = __ldg(src + r * lds + c);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int64_t c = c0 + threadIdx.y + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[c * ldd + r] = t[threadIdx.x][threadIdx.y + i];
+  }
+}
+
 // Two packed arrays in one launch (A and B of a BF16-mode call), eight elements per step.
 __global__ void convert_bf16_two_vec8_kernel(const float4 *__restrict__ x1, uint4 *__restrict__ y1, int64_t n1_8,
                                              const float4 *__restrict__ x2, uint4 *__restrict__ y2, int64_t n2_8) {
@@ -343,6 +362,15 @@ cudaError_t launch_convert_rows_bf16(const float *src, int64_t lds, uint16_t *ds
   else
     convert_rows_bf16_kernel<<<grid_for(M * N, 256), 256, 0, stream>>>(src, lds, reinterpret_cast<__nv_bfloat16 *>(dst),
                                                                        ldd, M, N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_transpose_f32(const float *src, int64_t lds, float *dst, int64_t ldd, int64_t rows, int64_t cols,
+                                 cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  if ((cols + 31) / 32 > 0x7FFFFFFF || (rows + 31) / 32 > 65535) return cudaErrorInvalidValue;
+  transpose_f32_kernel<<<dim3((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32)), dim3(32, 8), 0, stream>>>(
+      src, lds, dst, ldd, rows, cols);
   return cudaGetLastError();
 }
 

@@ -539,6 +539,28 @@ def test_bf16_output_matches_f32_then_convert(gpu, case):
     assert bool(torch.isnan(out16[0, :n].float()).all())
 
 
+@pytest.mark.parametrize("workload", ["mbr", "matmul", "matmul_add"])
+@pytest.mark.parametrize("cfg", [(3, 0, 0, 0, 1), (3, 0, 0, 1, 0), (3, 0, 0, 0, 3)],
+                         ids=["pair", "persistent", "pair-split3"])
+@pytest.mark.parametrize("shape", [(700, 900, 300), (2600, 2400, 96)], ids=lambda s: "x".join(map(str, s)))
+def test_tf32_transposed_b_within_bound_and_bitwise(gpu, workload, cfg, shape):
+    """TF32 with B read from a transposed, K-major copy (b_layout = 2): within the TF32
+    bound, and bit for bit the result of reading B as given (b_layout = 1) -- the same
+    products in the same order; ragged M and N, a K tail, every epilogue, split-K."""
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 47)
+    outs = []
+    for layout in (1, 2):
+        _lib.set_config(*cfg, b_layout=layout)
+        try:
+            outs.append(tg.run_op(workload, ins, m, n, k, "tf32"))
+        finally:
+            _lib.set_config()
+    res = tc.check_output(workload, ins, outs[1], "tf32")
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+
+
 def _bf16_rne_bits(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even f32 -> bf16 bit patterns (NaNs left to the caller)."""
     u = x.view(np.uint32).astype(np.uint64)
