@@ -6,7 +6,7 @@
 // the library's C-ABI (include/tforge.h), which picks and launches the sm_100a kernel.
 //
 //   tforge-gpu-bench --mode lib --workload mbr --m M --n N --k K [--precision fp32|tf32|bf16|fp32_exact]
-//       [--kernel pair|cta|simt --bn 256 --stages 4 --split S --persistent] [--warmup 10 --reps 100 --flush]
+//       [--kernel pair|cta|simt --bn 256 --stages 4 --split S --persistent --b-layout L] [--warmup 10 --reps 100 --flush]
 //       [--in-dir d --out o.bin] [--seed S]
 //   tforge-gpu-bench --mode cublas --workload mbr --m M --n N --k K
 //       [--math default|tf32|bf16|bf16x9|lt|lt_tf32]
@@ -64,7 +64,7 @@ void blas_ok(cublasStatus_t r, const char *what) {
 struct Args {
   std::string mode = "lib", workload, inDir, out, precision = "fp32", math = "default", kernel;
   long m = 0, n = 0, k = 0;
-  int warmup = 10, reps = 100, bn = 0, stages = 0, split = 0, persistent = 0;
+  int warmup = 10, reps = 100, bn = 0, stages = 0, split = 0, persistent = 0, b_layout = 0;
   bool flush = false, infoOnly = false;
   unsigned seed = 1234;
 };
@@ -89,6 +89,7 @@ Args parse(int argc, char **argv) {
     else if (f == "--stages") a.stages = std::stoi(next());
     else if (f == "--split") a.split = std::stoi(next());
     else if (f == "--persistent") a.persistent = 1;
+    else if (f == "--b-layout") a.b_layout = std::stoi(next());
     else if (f == "--warmup") a.warmup = std::stoi(next());
     else if (f == "--reps") a.reps = std::stoi(next());
     else if (f == "--flush") a.flush = true;
@@ -197,15 +198,16 @@ int main(int argc, char **argv) {
   const int mode = precision_mode(a.precision);
   const bool gemm = wl <= TFORGE_MATMUL_ADD;
 
-  if (a.bn || a.stages || a.split || a.persistent || !a.kernel.empty()) {
+  if (a.bn || a.stages || a.split || a.persistent || a.b_layout || !a.kernel.empty()) {
     // --kernel pair|cta|simt forces a kernel family (offline tuning); --bn/--stages refine it;
     // --split S sets the pair kernel's split-K factor and --persistent picks the persistent
     // pair kernel (both imply --kernel pair).
     int kind = 1;
     if (a.kernel == "pair" || ((a.split || a.persistent) && a.kernel.empty())) kind = 3;
+    else if (a.kernel.empty() && !a.bn && !a.stages) kind = 0;  // --b-layout alone: the table's kernel
     else if (a.kernel == "simt") kind = 2;
     else if (!a.kernel.empty() && a.kernel != "cta") die("--kernel pair|cta|simt");
-    tforge_config cfg{kind, a.bn, a.stages, a.persistent, a.split};
+    tforge_config cfg{kind, a.bn, a.stages, a.persistent, a.split, a.b_layout};
     tf_ok(tforge_set_config(&cfg), "tforge_set_config");
   }
   tforge_launch L{};

@@ -79,7 +79,8 @@ def parse_options(options: str) -> dict:
     opts = dict(o.split("=", 1) for o in options.split() if "=" in o)
     return {"precision": opts.get("precision", "fp32"), "bn": int(opts.get("bn", 0)),
             "stages": int(opts.get("stages", 0)), "kernel": opts.get("kernel", ""),
-            "split": int(opts.get("split", 0)), "persistent": int(opts.get("persistent", 0))}
+            "split": int(opts.get("split", 0)), "persistent": int(opts.get("persistent", 0)),
+            "b_layout": int(opts.get("b_layout", 0))}
 
 
 def _forced_kind(o: dict) -> int:
@@ -107,12 +108,12 @@ def compile_kernel(workload, m, n, k, options="", tag="default"):
     d = ART / tag / f"{workload}_{m}x{n}x{k}"
     d.mkdir(parents=True, exist_ok=True)
     kind = _forced_kind(o)
-    if kind:
-        _lib.set_config(kind, o["bn"], o["stages"], o.get("persistent", 0), o.get("split", 0))
+    if kind or o.get("b_layout"):
+        _lib.set_config(kind, o["bn"], o["stages"], o.get("persistent", 0), o.get("split", 0), o.get("b_layout", 0))
     try:
         desc = _lib.describe(workload, m, n, k or 0, o["precision"])
     finally:
-        if kind:
+        if kind or o.get("b_layout"):
             _lib.set_config()
     args = {"matmul": ["arg0", "arg1", "arg2"], "mbr": ["arg0", "arg1", "arg2", "arg3"],
             "matmul_add": ["arg0", "arg1", "arg2", "arg3"], "bias_add": ["arg0", "arg1", "arg2"],
@@ -141,6 +142,8 @@ def _bench_cmd(workload, m, n, k, kdir=None, launch=None, mode="kernel"):
             cmd += ["--split", o["split"]]
         if o.get("persistent"):
             cmd += ["--persistent"]
+        if o.get("b_layout"):
+            cmd += ["--b-layout", o["b_layout"]]
     return cmd
 
 
@@ -195,8 +198,8 @@ def run_op(workload: str, ins: dict, m: int, n: int, k: int | None, precision: s
     _lib.check(L.tforge_memset(out.ptr, 0xFF, m * n * 4, None), "memset")  # NaN prefill
     o = parse_options(options)
     kind = _forced_kind(o)
-    if kind:
-        _lib.set_config(kind, o["bn"], o["stages"], o.get("persistent", 0), o.get("split", 0))
+    if kind or o.get("b_layout"):
+        _lib.set_config(kind, o["bn"], o["stages"], o.get("persistent", 0), o.get("split", 0), o.get("b_layout", 0))
     try:
         if workload in tc.GEMM_WORKLOADS:
             _lib.gemm(workload, bufs["a"].addr, bufs["b"].addr, out.addr, m, n, k, precision,
@@ -213,7 +216,7 @@ def run_op(workload: str, ins: dict, m: int, n: int, k: int | None, precision: s
         _lib.check(_lib.device_status(None), "device status")
         return out.download((m, n))
     finally:
-        if kind:
+        if kind or o.get("b_layout"):
             _lib.set_config()
         for b in bufs.values():
             b.free()

@@ -261,3 +261,12 @@ def test_autotune_table_round_trip(tmp_path):
     out = tmp_path / "t.inc"
     autotune.write_table(entries, out)
     assert autotune.read_table(out) == entries
+
+
+def test_option_strings_carry_pair_kernel_knobs():
+    """compile_kernel / check / bench option strings reach tforge_config: persistent, split
+    and b_layout imply the pair kernel except b_layout alone, which keeps the table's."""
+    o = tg.parse_options("precision=tf32 kernel=pair persistent=1 split=0 b_layout=2")
+    assert (o["persistent"], o["b_layout"], tg._forced_kind(o)) == (1, 2, 3)
+    assert tg._forced_kind(tg.parse_options("b_layout=1")) == 0
+    assert tg._forced_kind(tg.parse_options("split=4")) == 3
