@@ -171,7 +171,7 @@ typedef struct tforge_config {
   int32_t split_k;       /* CTA-pair kernel in fp32 / TF32 mode: 0 = automatic, 1 = no split,
                             S = 2..8 pairs per tile, each over K / S */
   int32_t b_layout;      /* TF32 mode, 256-wide pair and persistent pair kernels: 0 = automatic
-                            (a transposed, K-major copy of B when M >= 16384), 1 = B as given,
+                            (a transposed, K-major copy of B when M >= 16384 and K >= 4096), 1 = B as given,
                             2 = always the transposed copy */
 } tforge_config;
 

@@ -405,14 +405,15 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   // TF32 with many rows: the MMAs read a transposed (K-major) copy of B, which the tensor
   // core takes faster than the row-major (MN-major) original; the transpose is one pass over
   // B, amortised over M.  Measured (interleaved, same box): 16384 x 8192 x 8192 +3 to +10 %,
-  // 65536 x 8192 x 8192 +2 to +6 %; 8192^3 even; 4096^3 and 8192 x 4096 x 1024 slower.
+  // 65536 x 8192 x 8192 +2 to +6 %; 8192^3 even; 4096^3 and 8192 x 4096 x 1024 slower (short
+  // K loops gain less from the K-major read), hence M >= 16384 and K >= 4096.
   int b_layout = 0;
   {
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     b_layout = g_cfg.b_layout;
   }
   const bool bkm = !bf16 && cfg.prec == PREC_TF32 && ((cfg.pair && cfg.bn == 256) || cfg.persist) && a->K % 4 == 0 &&
-                   (b_layout == 2 || (b_layout == 0 && a->M >= 16384));
+                   (b_layout == 2 || (b_layout == 0 && a->M >= 16384 && a->K >= 4096));
   void *bt = nullptr;
   if (bkm) {
     cudaMemPool_t pool = nullptr;
