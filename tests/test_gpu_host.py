@@ -126,3 +126,15 @@ def test_host_bf16_matches_device_entry(gpu):
     assert np.array_equal(bits(host), bits(dev))
     res = tc.check_output("mbr", ins, host, "bf16")
     assert res["err_over_bound"] <= 1.0, res
+
+
+@pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
+@pytest.mark.parametrize("workload", ["mbr", "matmul_add"])
+def test_host_wide_ragged_pitched_within_bound(gpu, workload, mode):
+    """A wide, ragged problem through the host entry: several row chunks, N not a multiple
+    of the tile width, pitched host rows, every tensor-core mode."""
+    m, n, k = 1500, 1304, 256
+    ins = tc.make_inputs(workload, m, n, k, 19)
+    out = run_host(workload, ins, m, n, k, mode, pitch=4)
+    res = tc.check_output(workload, ins, out, mode)
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
