@@ -412,16 +412,23 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     b_layout = g_cfg.b_layout;
   }
-  const bool bkm = !bf16 && cfg.prec == PREC_TF32 && ((cfg.pair && cfg.bn == 256) || cfg.persist) && a->K % 4 == 0 &&
-                   (b_layout == 2 || (b_layout == 0 && a->M >= 16384 && a->K >= 4096));
+  bool bkm = !bf16 && cfg.prec == PREC_TF32 && ((cfg.pair && cfg.bn == 256) || cfg.persist) && a->K % 4 == 0 &&
+             a->K <= 65535 * 32 &&  // the transpose kernel's grid
+             (b_layout == 2 || (b_layout == 0 && a->M >= 16384 && a->K >= 4096));
   void *bt = nullptr;
   if (bkm) {
     cudaMemPool_t pool = nullptr;
     rc = scratch_pool(&pool);
     if (rc) return rc;
     cudaError_t e2 = cudaMallocFromPoolAsync(&bt, sizeof(float) * (size_t)a->N * a->K, pool, st);
-    if (e2 != cudaSuccess) return cuda_fail(e2, "cudaMallocFromPoolAsync(transposed B)");
-    e2 = launch_transpose_f32(static_cast<const float *>(B), ldb, static_cast<float *>(bt), a->K, a->K, a->N, st);
+    if (e2 != cudaSuccess) {  // no room for the copy: read B as given
+      cudaGetLastError();
+      bt = nullptr;
+      bkm = false;
+    }
+  }
+  if (bkm) {
+    cudaError_t e2 = launch_transpose_f32(static_cast<const float *>(B), ldb, static_cast<float *>(bt), a->K, a->K, a->N, st);
     if (e2 == cudaSuccess) rc = make_tmap(&tmB, bt, false, a->N, a->K, a->K, bk, 128);
     if (e2 != cudaSuccess || rc) {
       cudaFreeAsync(bt, st);
