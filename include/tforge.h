@@ -177,9 +177,10 @@ typedef struct tforge_config {
 
 int tforge_set_config(const tforge_config *cfg);
 
-/* Synchronizes `stream`, then returns and clears the device status word that bounded
- * waits write on expiry (TFORGE_OK or TFORGE_ERR_TIMEOUT); TFORGE_ERR_CUDA if the
- * synchronization itself failed. */
+/* Synchronizes `stream`, then returns and clears the current device's status words that
+ * bounded waits write on expiry (TFORGE_OK or TFORGE_ERR_TIMEOUT): the one of the GEMM
+ * entries and the one of tforge_mbr_bf16_noalloc.  Allocates nothing.  TFORGE_ERR_CUDA if
+ * the synchronization itself failed. */
 int tforge_device_status(void *stream);
 
 /* Device-side wait limit in nanoseconds (default 1e9); 0 restores the default. */
@@ -188,6 +189,11 @@ int tforge_set_wait_limit_ns(uint64_t ns);
 /* Test hook: 1 makes the next GEMM launches' producer skip its first stage's load, so
  * the consumer's bounded wait expires and reports TFORGE_ERR_TIMEOUT; 0 clears. */
 int tforge_debug_skip_load(int on);
+
+/* Test hook: bytes of the library's scratch pool in use now and the high-water mark since
+ * the last reset (reset_high = 1 resets it after reading).  Creates the pool if the
+ * device has none yet. */
+int tforge_debug_pool_usage(uint64_t *used_now, uint64_t *used_high, int reset_high);
 
 const char *tforge_status_string(int status);
 const char *tforge_last_error(void);   /* text of the last TFORGE_ERR_CUDA, per thread */

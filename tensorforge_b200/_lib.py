@@ -68,6 +68,7 @@ SIGNATURES = {
     "tforge_device_status": (_I, [_P]),
     "tforge_set_wait_limit_ns": (_I, [_U64]),
     "tforge_debug_skip_load": (_I, [_I]),
+    "tforge_debug_pool_usage": (_I, [C.POINTER(_U64), C.POINTER(_U64), _I]),
     "tforge_status_string": (C.c_char_p, [_I]),
     "tforge_last_error": (C.c_char_p, []),
     "tforge_version": (C.c_char_p, []),
@@ -157,3 +158,10 @@ def gemm_host(workload: str, A: int, B: int, out: int, M: int, N: int, K: int, m
 
 def device_status(stream: int | None = None) -> int:
     return lib().tforge_device_status(stream)
+
+
+def pool_usage(reset_high: bool = False) -> tuple[int, int]:
+    """(bytes in use now, high-water mark) of the library's scratch pool on the current device."""
+    now, high = C.c_uint64(), C.c_uint64()
+    check(lib().tforge_debug_pool_usage(C.byref(now), C.byref(high), int(reset_high)), "tforge_debug_pool_usage")
+    return now.value, high.value

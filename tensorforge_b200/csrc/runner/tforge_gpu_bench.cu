@@ -143,19 +143,32 @@ __global__ void to_bf16(const float *x, __nv_bfloat16 *y, long n) {
   if (i < n) y[i] = __float2bfloat16_rn(x[i]);
 }
 
-struct Stats {
-  double median, min, mean, sd;
+// Per-rep samples reduced to the JSON's figures: median (mean of the two middle samples when
+// the count is even), minimum, mean and sample standard deviation (Welford's running update);
+// all -1 for no samples.
+struct Summary {
+  double median = -1, min = -1, mean = -1, sd = -1;
 };
-Stats stats(std::vector<double> v) {
-  if (v.empty()) return {-1, -1, -1, -1};
-  std::sort(v.begin(), v.end());
-  size_t n = v.size();
-  double mean = 0, var = 0;
-  for (double x : v) mean += x;
-  mean /= n;
-  for (double x : v) var += (x - mean) * (x - mean);
-  double med = n % 2 ? v[n / 2] : 0.5 * (v[n / 2 - 1] + v[n / 2]);
-  return {med, v.front(), mean, n > 1 ? std::sqrt(var / (n - 1)) : 0.0};
+Summary summarize(const std::vector<double> &samples) {
+  Summary r;
+  const size_t n = samples.size();
+  if (n == 0) return r;
+  std::vector<double> work(samples);
+  auto mid = work.begin() + n / 2;
+  std::nth_element(work.begin(), mid, work.end());
+  r.median = (n & 1) ? *mid : 0.5 * (*mid + *std::max_element(work.begin(), mid));
+  r.min = *std::min_element(samples.begin(), samples.end());
+  double mean = 0, m2 = 0;
+  size_t count = 0;
+  for (double x : samples) {
+    ++count;
+    const double d = x - mean;
+    mean += d / count;
+    m2 += d * (x - mean);
+  }
+  r.mean = mean;
+  r.sd = n > 1 ? std::sqrt(m2 / (n - 1)) : 0.0;
+  return r;
 }
 
 void fill(std::vector<float> &v, const Args &a, const char *name, std::mt19937 &rng) {
@@ -406,7 +419,7 @@ int main(int argc, char **argv) {
     if (nv.ok && nv.power(nv.dev, &p) == 0) pwr.push_back(p / 1000.0);
   }
   if (a.mode == "lib") tf_ok(tforge_device_status(stream), "device status");
-  Stats s = stats(ms), c = stats(clk), p = stats(pwr);
+  const Summary s = summarize(ms), c = summarize(clk), p = summarize(pwr);
   double clkMax = clk.empty() ? -1 : *std::max_element(clk.begin(), clk.end());
   int driver = 0;
   cudaDriverGetVersion(&driver);

@@ -92,6 +92,17 @@ constexpr int kMaxDev = 64;
 uint32_t *g_status[kMaxDev] = {};
 std::mutex g_status_mu;
 
+// The status word of the current device if a GEMM has created it, else nullptr (no allocation).
+uint32_t *existing_status_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  return g_status[dev];
+}
+
 int status_word(uint32_t **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -354,9 +365,10 @@ int device_pairs() {
 
 // Split-K factor of the CTA-pair kernel: tforge_config.split_k when set, else (fp32 and TF32
 // modes) as many pairs per tile as fit one wave of SM pairs, at most 8 and at least 4
-// k-blocks each; BF16 never splits (so the allocation-free BF16 entry matches it).
+// k-blocks each.  BF16 never splits, forced or not (so the allocation-free BF16 entry, which
+// has no workspace for partial sums, gives the same bits as tforge_mbr).
 int pair_splits(const TcConfig &c, int64_t M, int64_t N, int64_t K) {
-  if (!c.pair) return 1;
+  if (!c.pair || c.prec == PREC_BF16) return 1;
   {
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     if (g_cfg.kernel == 3 && g_cfg.split_k > 0) return g_cfg.split_k;
@@ -473,7 +485,8 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
     cudaFreeAsync(ws, st);
   } else if (cfg.persist) {
     CUtensorMap tmO;
-    rc = make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, ob16 ? SW64 : SW128);
+    rc = !bkm && persist_transposed(cfg.prec) ? make_tmap(&tmO, a->out, false, a->M, a->N, ldc, 128, 32, SWNONE)
+                                               : make_tmap(&tmO, a->out, ob16, a->M, a->N, ldc, 32, 128, ob16 ? SW64 : SW128);
     if (rc) return rc;
     e = launch_gemm_pair_persistent(cfg.prec, cfg.stages, epi, tmA, tmB, tmO, p, st);
   } else if (cfg.pair) {
@@ -520,6 +533,9 @@ int check_gemm_args(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64
 }
 
 int device_pool(cudaMemPool_t *out) { return scratch_pool(out); }
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(); }
+int debug_skip_load() { return g_debug_skip.load(); }
 
 }  // namespace tf
 
@@ -793,17 +809,22 @@ int tforge_set_config(const tforge_config *cfg) {
 int tforge_device_status(void *stream) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-  uint32_t *w = nullptr;
-  int rc = status_word(&w);
-  if (rc) return rc;
+  // Two words per device: the one tforge_gemm's kernels write (created by the first GEMM; a
+  // device without one has nothing to report, and nothing is allocated here) and the one in
+  // the allocation-free entry's static array.  Both are read and cleared.
   uint32_t v = 0;
-  e = cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
-  if (v) {
-    e = cudaMemset(w, 0, 4);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+  if (uint32_t *w = existing_status_word()) {
+    e = cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+    if (v) {
+      e = cudaMemset(w, 0, 4);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+    }
   }
-  return (int)v;
+  uint32_t v2 = 0;
+  const int rc = noalloc_take_status(&v2);
+  if (rc) return rc;
+  return (int)(v ? v : v2);
 }
 
 int tforge_set_wait_limit_ns(uint64_t ns) {
@@ -814,6 +835,20 @@ int tforge_set_wait_limit_ns(uint64_t ns) {
 int tforge_debug_skip_load(int on) {
   g_debug_skip.store(on ? 1 : 0);
   return TFORGE_OK;
+}
+
+int tforge_debug_pool_usage(uint64_t *used_now, uint64_t *used_high, int reset_high) {
+  if (!used_now || !used_high) return TFORGE_ERR_NULL;
+  cudaMemPool_t pool = nullptr;
+  int rc = scratch_pool(&pool);
+  if (rc) return rc;
+  cudaError_t e = cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, used_now);
+  if (e == cudaSuccess) e = cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemHigh, used_high);
+  if (e == cudaSuccess && reset_high) {
+    uint64_t zero = 0;
+    e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &zero);
+  }
+  return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "cudaMemPoolGetAttribute");
 }
 
 const char *tforge_status_string(int s) {

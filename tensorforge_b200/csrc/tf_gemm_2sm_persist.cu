@@ -17,6 +17,13 @@
 //     relu -> one of two dedicated 128 x 32 staging boxes (128-B swizzle) -> TMA store.
 //     The ring cannot lend its memory to the output here, since the next tile's loads
 //     are already in it.  matmul_add reads C_res with plain global loads.
+//   * TF32 with B as given (SWAP): the MMA's operands are exchanged as in the pair kernel --
+//     B's tile (MN-major, which for 32-bit elements the tensor core reads through the
+//     128B_BASE32B swizzle) is the M side, local to each CTA, and A's tile the N side shared
+//     by the pair -- so CTA r accumulates the transposed tile: TMEM lane = output column
+//     n0 + 128 r + lane, TMEM column j = output row (pair's first row) + j.  Each 32-column
+//     chunk is 32 output rows x 128 columns, staged row-major without swizzle (a warp writes
+//     128 consecutive bytes per row) and stored as one 32-row x 128-column TMA box.
 //
 // 256 threads: warp 0 TMA producer (both CTAs), warp 1 MMA issuer (leader), warps 4..7
 // epilogue.  Every wait is bounded (tf_ptx.cuh); on a timeout each role stops, the MMA
@@ -31,6 +38,12 @@
 namespace tf {
 
 namespace {
+
+#ifndef TF_PERSIST_SWAP
+#define TF_PERSIST_SWAP 0
+#endif
+// TF32 with B as given: exchange the MMA's operands (see the kernel's header comment).
+constexpr bool kPersistSwap = TF_PERSIST_SWAP;
 
 template <int PREC, int STAGES>
 struct PersistLayout {
@@ -70,8 +83,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                                 const __grid_constant__ CUtensorMap tmO, const TcParams p) {
   using L = PersistLayout<PREC, STAGES>;
   constexpr bool kTF32 = PREC == PREC_TF32;
+  // TF32 with B as given: operands exchanged, transposed accumulator and epilogue.
+  constexpr bool kSwap = kTF32 && !BKM && kPersistSwap;
   // BKM (TF32): B is a transposed copy, loaded and read K-major like A.
-  constexpr uint32_t kIdesc = BKM ? (instr_desc(2u, 256, 256) & ~(1u << 16)) : instr_desc(kTF32 ? 2u : 1u, 256, 256);
+  constexpr uint32_t kIdesc = kSwap  ? instr_desc_a_mn(2u, 256, 256)
+                              : BKM ? (instr_desc(2u, 256, 256) & ~(1u << 16))
+                                    : instr_desc(kTF32 ? 2u : 1u, 256, 256);
   // bf16 output (OUTB): BF16 precision and the mbr epilogue only.
   static_assert(!OUTB || (PREC == PREC_BF16 && EPI == EPI_MBR), "bf16 output configuration");
   static_assert(!BKM || PREC == PREC_TF32, "K-major B configuration");
@@ -194,7 +211,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           const uint64_t ad = smem_desc(slot + ks * 32, 16, 1024, 2);
           const uint64_t bd = BKM ? smem_desc(slot + L::kABytes + ks * 32, 16, 1024, 2)
                                   : smem_desc(slot + L::kABytes + ks * L::kUmmaK * 128, L::kBK * 128, L::kBSbo, L::kBSwz);
-          mma_ss_pair<kTF32>(acc, ad, bd, kIdesc, (kb | ks) ? 1u : 0u);
+          if constexpr (kSwap)
+            mma_ss_pair<kTF32>(acc, bd, ad, kIdesc, (kb | ks) ? 1u : 0u);
+          else
+            mma_ss_pair<kTF32>(acc, ad, bd, kIdesc, (kb | ks) ? 1u : 0u);
         }
         mma_commit_pair(empty0 + 8 * s, 0x3);
       }
@@ -235,6 +255,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       tc_fence_after();
       const bool cta_rows = m0 < p.M;
       const uint32_t tacc = tmem + 256u * b + ((uint32_t)(q * 32) << 16);
+      if constexpr (kSwap) {
+        // Transposed accumulator: thread r holds output column nb + r for the pair's 256 rows
+        // mp0 .., 32 per chunk; chunk c goes through box c % 2 (32 rows x 128 columns).
+        const int mp0 = tm * 256, nb = n0 + (int)rank * 128, col = nb + r;
+        const bool cta_cols = nb < p.N;
+        const float bcol = EPI == EPI_MBR ? reinterpret_cast<const float *>(bias_s)[(int)rank * 128 + r] : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          const int row0 = mp0 + 32 * c;
+          const bool live = cta_cols && row0 < p.M;
+          uint32_t rr[32];
+          tmem_ld_32x32b_x32(tacc + c * 32, rr);
+          float cr[32];
+          if constexpr (EPI == EPI_ADD) {
+            const bool col_ok = live && col < p.N;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              cr[i] = col_ok && row0 + i < p.M ? __ldg(p.cres + (int64_t)(row0 + i) * p.ldc + col) : 0.f;
+          }
+          tmem_ld_wait(rr);
+          float *box = reinterpret_cast<float *>(boxes + (c & 1) * L::kBoxBytes);
+          if (et == 0) bulk_wait_group_read1();
+          named_barrier(2, 128);
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float v = __uint_as_float(rr[i]);
+              if constexpr (EPI == EPI_MBR) v = relu_ieee(__fadd_rn(v, bcol));
+              else if constexpr (EPI == EPI_ADD) v = __fadd_rn(v, cr[i]);
+              box[i * 128 + r] = v;
+            }
+          }
+          fence_proxy_async_smem();
+          named_barrier(3, 128);
+          if (et == 0 && live) {
+            tma_store_2d(&tmO, smem_u32(box), nb, row0);
+            bulk_commit_group();
+          }
+        }
+      } else {
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
         const int col0 = n0 + c * 32;
@@ -297,6 +357,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           tma_store_2d(&tmO, smem_u32(box), col0, m0);
           bulk_commit_group();
         }
+      }
       }
       // Every tcgen05.ld of accumulator b has completed (tmem_ld_wait): release it.
       tc_fence_before();
@@ -412,6 +473,8 @@ cudaError_t persist_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
 
 // Instantiated persistent configurations: (precision, stages).
 #define TF_PERSIST_CONFIGS(X) X(PREC_TF32, 6) X(PREC_BF16, 6)
+
+bool persist_transposed(int prec) { return prec == PREC_TF32 && kPersistSwap; }
 
 int persist_smem_bytes(int prec, int stages) {
 #define TF_PSMEM(P, S) \

@@ -103,6 +103,9 @@ cudaError_t launch_gemm_pair_persistent(int prec, int stages, int epi, const CUt
 cudaError_t persist_func_attributes(int prec, int stages, int epi, cudaFuncAttributes *attr,
                                     int *blocks_per_sm);
 int persist_grid_pairs(int prec, int stages, int epi, int64_t M, int64_t N);
+// True when the persistent kernel for `prec` accumulates the transposed tile (TF32 reading B as
+// given): its output map then uses 32-row x 128-column boxes without swizzle.
+bool persist_transposed(int prec);
 
 // The dispatch table's tensor-core choice (false when it would not use tcgen05), the
 // TMA operand map encoder, and the per-thread error text (all defined in tf_api.cu).
@@ -117,6 +120,13 @@ void set_last_error(const char *msg);
 // library's per-device stream-ordered memory pool.
 int check_gemm_args(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *ldc);
 int device_pool(cudaMemPool_t *out);
+// The bounded-wait limit (tforge_set_wait_limit_ns) and the skip-load test hook
+// (tforge_debug_skip_load) every GEMM launch passes to its kernel.
+uint64_t wait_limit_ns();
+int debug_skip_load();
+// Reads and clears the allocation-free entry's status word on the current device (tf_noalloc.cu);
+// *v = 0 when that entry was never set up on it.
+int noalloc_take_status(uint32_t *v);
 
 // SIMT sequential-k FFMA GEMM (bitwise equal to the reference's generated kernels).
 cudaError_t launch_gemm_simt(int epi, const float *A, const float *B, const float *aux, float *C,

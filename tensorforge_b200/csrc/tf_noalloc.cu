@@ -17,11 +17,16 @@
 //     most 16 MiB, e.g. M = N = K = 2048.  Larger problems are rejected with
 //     TFORGE_ERR_SHAPE and a message in tforge_last_error(); nothing is allocated instead.
 //   * All calls share the array and each call overwrites it, so calls that overlap on the
-//     GPU (on different streams without ordering between them) race.  The status word is
-//     cleared on the caller's stream at the start of every call.
+//     GPU (on different streams without ordering between them) race.
+//   * The kernels' bounded waits honour tforge_set_wait_limit_ns and tforge_debug_skip_load
+//     like every other GEMM entry.  A wait that expires writes TFORGE_ERR_TIMEOUT into the
+//     status word; tforge_device_status reports it (and clears it) with the other entries'
+//     status, so a call whose output is incomplete never goes unnoticed.  The word is
+//     cleared only when it is read.
 //   * In host code the array's name does not denote a device address.  The first call on
 //     each device resolves the address with cudaGetSymbolAddress (with that device
-//     current) and caches it; make that first call before any stream capture.
+//     current), clears the status word and caches the address; make that first call before
+//     any stream capture.
 //   * No cudaMalloc, cudaFree, pool or other allocating routine is called on this path.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -51,13 +56,22 @@ int scratch_address(void **out) {
     tf::set_last_error(cudaGetErrorString(e));
     return TFORGE_ERR_CUDA;
   }
-  if (dev < 0 || dev >= kMaxDevices) return TFORGE_ERR_UNSUPPORTED;
+  if (dev < 0 || dev >= kMaxDevices) {
+    tf::set_last_error("tforge_mbr_bf16_noalloc: device index beyond the 64 this library tracks");
+    return TFORGE_ERR_UNSUPPORTED;
+  }
   std::lock_guard<std::mutex> lk(g_addr_mu);
   if (!g_addr[dev]) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
       tf::set_last_error(e != cudaSuccess ? cudaGetErrorString(e) : "cudaGetSymbolAddress returned NULL");
+      return TFORGE_ERR_CUDA;
+    }
+    // Set-up: the status word starts at zero (cudaMemset allocates nothing).
+    e = cudaMemset(static_cast<unsigned char *>(p) + kScratchBytes, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) {
+      tf::set_last_error(cudaGetErrorString(e));
       return TFORGE_ERR_CUDA;
     }
     g_addr[dev] = p;
@@ -74,6 +88,33 @@ bool overlap(const void *a, size_t an, const void *b, size_t bn) {
 }
 
 }  // namespace
+
+namespace tf {
+
+int noalloc_take_status(uint32_t *v) {
+  *v = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return TFORGE_OK;
+  }
+  void *base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_addr_mu);
+    base = g_addr[dev];
+  }
+  if (!base) return TFORGE_OK;  // never set up on this device: nothing can have been written
+  uint32_t *w = reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(base) + kScratchBytes);
+  cudaError_t e = cudaMemcpy(v, w, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && *v) e = cudaMemset(w, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) {
+    set_last_error(cudaGetErrorString(e));
+    return TFORGE_ERR_CUDA;
+  }
+  return TFORGE_OK;
+}
+
+}  // namespace tf
 
 extern "C" int tforge_mbr_bf16_noalloc(const float *A, const float *B, const float *bias, float *out,
                                        int64_t M, int64_t N, int64_t K, void *stream) {
@@ -105,8 +146,7 @@ extern "C" int tforge_mbr_bf16_noalloc(const float *A, const float *B, const flo
   uint32_t *status = reinterpret_cast<uint32_t *>(static_cast<unsigned char *>(base) + kScratchBytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st);
-  if (e == cudaSuccess) e = tf::launch_convert_bf16(A, sa, M * K, st);
+  cudaError_t e = tf::launch_convert_bf16(A, sa, M * K, st);
   if (e == cudaSuccess) e = tf::launch_convert_bf16(B, sb, K * N, st);
   if (e != cudaSuccess) {
     tf::set_last_error(cudaGetErrorString(e));
@@ -125,8 +165,8 @@ extern "C" int tforge_mbr_bf16_noalloc(const float *A, const float *B, const flo
   p.K = (int32_t)K;
   p.ldc = N;
   p.status = status;
-  p.limit_ns = 1000000000ull;
-  p.debug_skip = 0;
+  p.limit_ns = tf::wait_limit_ns();
+  p.debug_skip = tf::debug_skip_load();
   if (cfg.pair) {
     CUtensorMap tmO;
     rc = tf::encode_operand_map(&tmO, out, false, M, N, N, 32, 128, false);

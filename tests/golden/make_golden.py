@@ -1,6 +1,6 @@
 """Regenerate tests/golden/golden.json from the reference tree (run where it exists).
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference tree>   (or TF_REFERENCE=<tree>)
 
 What it records, and from where:
 
@@ -27,6 +27,7 @@ import argparse
 import csv
 import hashlib
 import json
+import os
 import pathlib
 import shutil
 import subprocess
@@ -45,8 +46,11 @@ def sha(arr: np.ndarray) -> str:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TF_REFERENCE"),
+                    help="the reference source tree (default: $TF_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <reference tree> or set TF_REFERENCE")
     ref = pathlib.Path(args.reference)
     sys.path.insert(0, str(ref / "python"))
     import tforge_cpu as rtc  # the reference's host library (imports only numpy)
@@ -60,7 +64,7 @@ def main() -> int:
         shutil.copy(REPO / "oracle" / "build" / f"k_{workload}.so", d / "k.so")
         return d
 
-    golden: dict = {"source": "reference tree at " + str(ref) + " (values below are copied from it)"}
+    golden: dict = {"source": "the reference tree (NirakChoun/TensorForge sources; values below are copied from it)"}
 
     # Published E1 numerics.
     pins = []
