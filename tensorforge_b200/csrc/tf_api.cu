@@ -339,12 +339,13 @@ int check_gemm(const tforge_gemm_args *a, int64_t *lda, int64_t *ldb, int64_t *l
   return TFORGE_OK;
 }
 
-// TMA needs 16-byte-aligned bases and pitches; the vector epilogue needs 16-byte rows.
+// TMA needs 16-byte-aligned bases and pitches; the vector epilogue needs 16-byte rows.  In
+// BF16 mode an f32 operand is read once into a packed bf16 copy, so only its f32 rows need
+// 16 bytes; a bf16 operand's own rows are checked with its element size.
 bool tma_compatible(const tforge_gemm_args *a, int64_t lda, int64_t ldb, int64_t ldc) {
   const int ea = a->a_dtype == TFORGE_BF16 ? 2 : 4, eb = a->b_dtype == TFORGE_BF16 ? 2 : 4;
   const int eo = a->out_dtype == TFORGE_BF16 ? 2 : 4;
   if ((lda * ea) % 16 || (ldb * eb) % 16 || (ldc * eo) % 16) return false;
-  if (a->mode == TFORGE_MODE_BF16 && ((lda * 2) % 16 || (ldb * 2) % 16)) return false;
   if (!aligned(a->A, 16) || !aligned(a->B, 16) || !aligned(a->out, 16)) return false;
   if (a->workload == TFORGE_MBR && !aligned(a->bias, 16)) return false;
   if (a->workload == TFORGE_MATMUL_ADD && !aligned(a->C_res, 16)) return false;
@@ -389,7 +390,7 @@ int auto_pair_splits(int prec, int64_t M, int64_t N, int64_t K) {
 }
 
 int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const void *B,
-           bool bf16, int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t st) {
+           bool bf16, int64_t lda, int64_t ldb, int64_t ldc, cudaStream_t st, bool after_conversion = false) {
   const int esz = bf16 ? 2 : 4;
   const uint32_t bk = 128 / esz;  // K elements per stage
   CUtensorMap tmA, tmB;
@@ -411,6 +412,9 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   if (rc) return rc;
   p.limit_ns = g_wait_limit_ns.load();
   p.debug_skip = g_debug_skip.load();
+  // The operand conversion just launched on this stream wrote A and B: overlap this launch's
+  // set-up with its tail (programmatic dependent launch).
+  p.pdl = after_conversion ? 1 : 0;
   const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
   cudaError_t e;
   const int splits = pair_splits(cfg, a->M, a->N, a->K);
@@ -447,6 +451,7 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
       return rc ? rc : cuda_fail(e2, "B transpose");
     }
     p.b_kmajor = 1;
+    p.pdl = 1;  // the GEMM sets up while the transpose finishes
   }
   // The copy is released (stream-ordered) after the launches below, on every return path.
   struct PoolRelease {
@@ -646,7 +651,7 @@ int tforge_gemm(const tforge_gemm_args *a, void *stream) {
                                      a->K, lda, ldb, ldc, st);
     return e == cudaSuccess ? TFORGE_OK : cuda_fail(e, "SIMT GEMM launch");
   }
-  rc = run_tc(a, c.tc, A, B, true, la, lb, ldc, st);
+  rc = run_tc(a, c.tc, A, B, true, la, lb, ldc, st, scratch != nullptr);
   if (scratch) cudaFreeAsync(scratch, st);
   return rc;
 }

@@ -285,6 +285,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
+    grid_dependency_wait();  // operands written by the kernel before this launch (TcParams::pdl)
     // 3xTF32: loads complete on this CTA's full[l]; the slot is reused once this CTA's
     // converters have loaded it (lempty[l]).  TF32/BF16: loads complete on the LEADER's
     // full[l], which expects both CTAs' bytes; the slot is reused once the pair MMAs that
@@ -651,6 +652,12 @@ cudaError_t launch_pair_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, con
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
   dim3 grid(2 * ((p.N + BN - 1) / BN), (p.M + 255) / 256, p.splits > 1 ? p.splits : 1);
+  if (p.pdl) {
+    cudaLaunchAttribute attr[1];
+    pdl_attr(attr[0]);
+    cudaLaunchConfig_t cfg = {grid, dim3(L::kThreads), (size_t)L::kSmemBytes, stream, attr, 1};
+    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, tmC, p);
+  }
   kern<<<grid, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, tmO, tmC, p);
   return cudaGetLastError();
 }

@@ -40,7 +40,7 @@ namespace tf {
 namespace {
 
 #ifndef TF_PERSIST_SWAP
-#define TF_PERSIST_SWAP 0
+#define TF_PERSIST_SWAP 1
 #endif
 // TF32 with B as given: exchange the MMA's operands (see the kernel's header comment).
 constexpr bool kPersistSwap = TF_PERSIST_SWAP;
@@ -146,6 +146,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
+    grid_dependency_wait();  // operands written by the kernel before this launch (TcParams::pdl)
     // Loads complete on the LEADER's full[s], which expects both CTAs' bytes; slot s is
     // reused once the pair MMAs that read it are done (empty[s], committed to both CTAs).
     const uint32_t lead_full0 = map_to_cta(full0, 0);
@@ -423,8 +424,14 @@ cudaError_t launch_persist_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, 
   if (clusters <= 0) return cudaErrorInvalidConfiguration;
   const int64_t tiles = (int64_t)((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int pairs = tiles < clusters ? (int)tiles : clusters;
-  gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM><<<2 * pairs, L::kThreads, L::kSmemBytes, stream>>>(
-      tmA, tmB, tmO, p);
+  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM>;
+  if (p.pdl) {
+    cudaLaunchAttribute attr[1];
+    pdl_attr(attr[0]);
+    cudaLaunchConfig_t cfg = {dim3(2 * pairs), dim3(L::kThreads), (size_t)L::kSmemBytes, stream, attr, 1};
+    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmO, p);
+  }
+  kern<<<2 * pairs, L::kThreads, L::kSmemBytes, stream>>>(tmA, tmB, tmO, p);
   return cudaGetLastError();
 }
 

@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
+    grid_dependency_wait();  // operands written by the kernel before this launch (TcParams::pdl)
     int kb = 0;
     for (; kb < nkb; ++kb) {
       const int s = kb % STAGES, round = kb / STAGES;
@@ -260,6 +261,12 @@ static cudaError_t launch_one(const CUtensorMap &tmA, const CUtensorMap &tmB, co
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
   dim3 grid((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM, 1);
+  if (p.pdl) {
+    cudaLaunchAttribute attr[1];
+    pdl_attr(attr[0]);
+    cudaLaunchConfig_t cfg = {grid, dim3(kThreads), (size_t)L::kSmemBytes, stream, attr, 1};
+    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p);
+  }
   kern<<<grid, kThreads, L::kSmemBytes, stream>>>(tmA, tmB, p);
   return cudaGetLastError();
 }

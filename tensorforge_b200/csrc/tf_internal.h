@@ -53,7 +53,18 @@ struct TcParams {
   // 1 (TF32, 256-wide pair tiles or the persistent pair kernel): tmB maps a transposed copy
   // of B (N x K, K-major tiles of 128 columns x 32 k); the MMAs read both operands K-major.
   int32_t b_kmajor;
+  // 1: the launch is a programmatic dependent of the kernel just before it on the stream (the
+  // operand conversion or B transpose that wrote what tmA / tmB read): the CTAs set up while
+  // that kernel finishes, and the TMA producer waits for it (griddepcontrol.wait) before its
+  // first operand load.  Nothing else in the GEMM reads what that kernel writes.
+  int32_t pdl;
 };
+
+// Launch attribute of a programmatic dependent launch (TcParams::pdl).
+inline void pdl_attr(cudaLaunchAttribute &a) {
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+}
 
 struct TcConfig {
   int prec;    // Prec

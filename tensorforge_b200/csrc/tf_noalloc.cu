@@ -167,6 +167,7 @@ extern "C" int tforge_mbr_bf16_noalloc(const float *A, const float *B, const flo
   p.status = status;
   p.limit_ns = tf::wait_limit_ns();
   p.debug_skip = tf::debug_skip_load();
+  p.pdl = 1;  // the conversions above wrote A and B: the GEMM sets up while they finish
   if (cfg.pair) {
     CUtensorMap tmO;
     rc = tf::encode_operand_map(&tmO, out, false, M, N, N, 32, 128, false);

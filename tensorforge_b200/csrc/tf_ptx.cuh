@@ -148,6 +148,13 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch.  grid_dependency_wait: block until the grid this launch
+// depends on has completed and its memory writes are visible (immediately, when the launch
+// had no programmatic dependency).  grid_launch_dependents: let the grids that depend on this
+// one start launching (their CTAs can set up while this grid finishes).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Generic-proxy writes to shared memory -> visible to the async proxy (tcgen05.mma).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

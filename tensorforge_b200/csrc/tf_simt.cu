@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include "tf_internal.h"
+#include "tf_ptx.cuh"
 
 namespace tf {
 
@@ -191,6 +192,7 @@ __global__ void elementwise_scalar(int op, const float *__restrict__ X, const fl
 
 __global__ void convert_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y,
                                     int64_t n) {
+  grid_launch_dependents();  // a GEMM launched as this kernel's dependent may start setting up
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     y[i] = __float2bfloat16_rn(x[i]);
@@ -206,6 +208,7 @@ __device__ __forceinline__ uint4 bf16x8(const float4 a, const float4 b) {
   return make_uint4(bf16x2_bits(a.x, a.y), bf16x2_bits(a.z, a.w), bf16x2_bits(b.x, b.y), bf16x2_bits(b.z, b.w));
 }
 __global__ void convert_bf16_vec8_kernel(const float4 *__restrict__ x, uint4 *__restrict__ y, int64_t n8) {
+  grid_launch_dependents();  // a GEMM launched as this kernel's dependent may start setting up
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = bf16x8(__ldg(x + 2 * i), __ldg(x + 2 * i + 1));
 }
@@ -214,6 +217,7 @@ __global__ void convert_bf16_vec8_kernel(const float4 *__restrict__ x, uint4 *__
 // bank conflicts), coalesced reads along c and writes along r; 32 x 8 threads, 4 rows each.
 __global__ void transpose_f32_kernel(const float *__restrict__ src, int64_t lds, float *__restrict__ dst, int64_t ldd,
                                      int64_t rows, int64_t cols) {
+  grid_launch_dependents();  // a GEMM launched as this kernel's dependent may start setting up
   __shared__ float t[32][33];
   const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
 #pragma unroll
@@ -232,6 +236,7 @@ __global__ void transpose_f32_kernel(const float *__restrict__ src, int64_t lds,
 // Two packed arrays in one launch (A and B of a BF16-mode call), eight elements per step.
 __global__ void convert_bf16_two_vec8_kernel(const float4 *__restrict__ x1, uint4 *__restrict__ y1, int64_t n1_8,
                                              const float4 *__restrict__ x2, uint4 *__restrict__ y2, int64_t n2_8) {
+  grid_launch_dependents();  // a GEMM launched as this kernel's dependent may start setting up
   const int64_t total = n1_8 + n2_8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     if (i < n1_8) y1[i] = bf16x8(__ldg(x1 + 2 * i), __ldg(x1 + 2 * i + 1));
@@ -245,6 +250,7 @@ __global__ void convert_bf16_two_vec8_kernel(const float4 *__restrict__ x1, uint
 // Pitched rows, eight elements per step (N, both pitches multiples of 8, bases aligned).
 __global__ void convert_rows_bf16_vec8_kernel(const float *__restrict__ x, int64_t lds, uint16_t *__restrict__ y,
                                               int64_t ldd, int64_t M, int64_t n8) {
+  grid_launch_dependents();  // a GEMM launched as this kernel's dependent may start setting up
   const int64_t total = M * n8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / n8, c = (i - r * n8) * 8;
@@ -256,6 +262,7 @@ __global__ void convert_rows_bf16_vec8_kernel(const float *__restrict__ x, int64
 // Pitched f32 -> bf16 rows (one element per thread step; the general bf16-output path).
 __global__ void convert_rows_bf16_kernel(const float *__restrict__ x, int64_t lds, __nv_bfloat16 *__restrict__ y,
                                          int64_t ldd, int64_t M, int64_t N) {
+  grid_launch_dependents();  // a GEMM launched as this kernel's dependent may start setting up
   const int64_t total = M * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / N, c = i - r * N;

@@ -614,6 +614,7 @@ def test_concurrent_streams_match_single_stream(gpu):
                   bias=t["bias"].data_ptr() if "bias" in t else None,
                   c_res=t["c"].data_ptr() if "c" in t else None, stream=stream.cuda_stream)
 
+    torch.cuda.synchronize()  # inputs uploaded on the default stream before the side streams read them
     ref = []
     s0 = torch.cuda.Stream()
     for i, (wl, m, n, k, mode, t) in enumerate(data):
@@ -623,6 +624,7 @@ def test_concurrent_streams_match_single_stream(gpu):
     torch.cuda.synchronize()
     streams = [torch.cuda.Stream(), torch.cuda.Stream()]
     outs = [[torch.full((m, n), float("nan"), device=dev) for (_, m, n, _, _, _) in data] for _ in range(4)]
+    torch.cuda.synchronize()  # the fills (default stream) finish before the side streams write
     for r in range(4):
         for i in range(len(data)):
             launch(i, streams[(r + i) % 2], outs[r][i])
