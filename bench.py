@@ -82,6 +82,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-config4", action="store_true",
                     help="skip the BASELINE config-4 measurement (131072x8192x8192 TF32, M-sharded)")
+    ap.add_argument("--nccl-debug", default="INFO",
+                    help="NCCL_DEBUG level for the communicator set-up lines on stderr (N > 1); off: leave the env")
     args = ap.parse_args()
     if args.shape:
         args.m, args.n, args.k = (int(x) for x in args.shape.lower().split("x"))
@@ -382,9 +384,11 @@ def ours(args):
     if world > 1:
         import datetime
 
-        # NCCL reports its communicator set-up (ranks, devices, NVLink/NVLS, channels) on stderr.
-        if "NCCL_DEBUG" not in os.environ:
-            os.environ.update({"NCCL_DEBUG": "INFO", "NCCL_DEBUG_SUBSYS": "INIT", "NCCL_DEBUG_FILE": "/dev/stderr"})
+        # NCCL reports its communicator set-up (ranks, devices, NVLink/NVLS, channels) on stderr
+        # (`--nccl-debug off` leaves the environment's NCCL_DEBUG settings as they are).
+        if args.nccl_debug != "off":
+            os.environ.update({"NCCL_DEBUG": args.nccl_debug, "NCCL_DEBUG_SUBSYS": "INIT",
+                               "NCCL_DEBUG_FILE": "/dev/stderr"})
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
     from tensorforge_b200.shard import broadcast_weights, row_partition
@@ -613,9 +617,11 @@ def config4_leg(L, _lib, tc, world, rank, local, dev, target_ms=200.0) -> dict |
     res = tc.check_output("mbr", {"a": A[idx].cpu().numpy(), "b": W.cpu().numpy(), "bias": bias.cpu().numpy()},
                           out[idx].cpu().numpy(), C4_MODE)
     launch = _lib.describe("mbr", m, n, k, C4_MODE)
+    props = torch.cuda.get_device_properties(dev)
+    gpu = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}"
     mine = {"rank": rank, "rows": m, "ms": ms, "broadcast_ms": bcast, "clocks": clk.summary(),
             "err_over_bound": res["err_over_bound"], "pass": bool(res["pass"]), "device_status": status,
-            "kernel": launch["kernel"]}
+            "kernel": launch["kernel"], "gpu_pci": gpu}
     ranks = [None] * world
     if world > 1:
         dist.all_gather_object(ranks, mine)
@@ -642,7 +648,8 @@ def config4_leg(L, _lib, tc, world, rank, local, dev, target_ms=200.0) -> dict |
                                                                           for r in ranks),
             "max_err_over_bound": max(r["err_over_bound"] for r in ranks),
             "nccl": ".".join(map(str, torch.cuda.nccl.version())) if world > 1 else None,
-            "per_rank": [{"rank": r["rank"], "rows": r["rows"], "ms_per_step": r["ms"] / steps,
+            "distinct_gpus": len({r["gpu_pci"] for r in ranks}),
+            "per_rank": [{"rank": r["rank"], "gpu_pci": r["gpu_pci"], "rows": r["rows"], "ms_per_step": r["ms"] / steps,
                           "sm_mhz": r["clocks"].get("sm_mhz"), "reasons": r["clocks"].get("reasons"),
                           "kernel": r["kernel"]} for r in ranks]}
 
