@@ -7,7 +7,9 @@
 //
 //   tforge-gpu-bench --mode lib --workload mbr --m M --n N --k K [--precision fp32|tf32|bf16|fp32_exact]
 //       [--kernel pair|cta|simt --bn 256 --stages 4 --split S --persistent --b-layout L] [--warmup 10 --reps 100 --flush]
-//       [--in-dir d --out o.bin] [--seed S]
+//       [--in-dir d --out o.bin] [--seed S] [--operands bf16]
+//     --operands bf16 (BF16 precision): A and B rounded to bf16 once before timing and passed
+//     as bf16 (tforge_gemm, a_dtype = b_dtype = TFORGE_BF16), so only the GEMM is timed.
 //   tforge-gpu-bench --mode cublas --workload mbr --m M --n N --k K
 //       [--math default|tf32|bf16|bf16x9|lt|lt_tf32]
 //     default: cublasSgemm (FP32 FMA) + separate bias/relu -- the reference's comparator;
@@ -62,7 +64,8 @@ void blas_ok(cublasStatus_t r, const char *what) {
 }
 
 struct Args {
-  std::string mode = "lib", workload, inDir, out, precision = "fp32", math = "default", kernel;
+  std::string mode = "lib", workload, inDir, out, precision = "fp32", math = "default", kernel,
+              operands = "f32";
   long m = 0, n = 0, k = 0;
   int warmup = 10, reps = 100, bn = 0, stages = 0, split = 0, persistent = 0, b_layout = 0;
   bool flush = false, infoOnly = false;
@@ -86,6 +89,7 @@ Args parse(int argc, char **argv) {
     else if (f == "--math") a.math = next();
     else if (f == "--bn") a.bn = std::stoi(next());
     else if (f == "--kernel") a.kernel = next();
+    else if (f == "--operands") a.operands = next();
     else if (f == "--stages") a.stages = std::stoi(next());
     else if (f == "--split") a.split = std::stoi(next());
     else if (f == "--persistent") a.persistent = 1;
@@ -284,7 +288,41 @@ int main(int argc, char **argv) {
   void *ltWs = nullptr;
   std::string kernel = L.kernel;
 
-  if (a.mode == "lib") {
+  // --operands bf16 (lib mode, BF16 precision, GEMM workloads): A and B are rounded to bf16
+  // once, before timing, and each call passes the bf16 copies (tforge_gemm with a_dtype =
+  // b_dtype = TFORGE_BF16), so only the GEMM is timed; the output is the same bits as the
+  // call on f32 operands.
+  if (a.operands != "f32" && a.operands != "bf16") die("--operands f32|bf16");
+  const bool bf16_ops = a.operands == "bf16";
+  if (bf16_ops && (a.mode != "lib" || !gemm || mode != TFORGE_MODE_BF16))
+    die("--operands bf16 needs --mode lib, a GEMM workload and --precision bf16");
+  if (bf16_ops) {
+    cuda_ok(cudaMalloc(&abf, M * K * 2), "cudaMalloc(A bf16)");
+    cuda_ok(cudaMalloc(&bbf, K * N * 2), "cudaMalloc(B bf16)");
+    tf_ok(tforge_convert_bf16(dA, reinterpret_cast<uint16_t *>(abf), M * K, stream), "tforge_convert_bf16(A)");
+    tf_ok(tforge_convert_bf16(dB, reinterpret_cast<uint16_t *>(bbf), K * N, stream), "tforge_convert_bf16(B)");
+    cuda_ok(cudaStreamSynchronize(stream), "convert");
+    kernel = L.kernel;
+  }
+
+  if (a.mode == "lib" && bf16_ops) {
+    run = [&] {
+      tforge_gemm_args g{};
+      g.workload = wl;
+      g.mode = mode;
+      g.a_dtype = TFORGE_BF16;
+      g.b_dtype = TFORGE_BF16;
+      g.A = abf;
+      g.B = bbf;
+      g.bias = dBias;
+      g.C_res = dRes;
+      g.out = dC;
+      g.M = M;
+      g.N = N;
+      g.K = K;
+      tf_ok(tforge_gemm(&g, stream), "tforge_gemm (bf16 operands)");
+    };
+  } else if (a.mode == "lib") {
     run = [&] {
       int rc = TFORGE_OK;
       switch (wl) {

@@ -139,3 +139,23 @@ def test_f32_operands_timeout_reported_and_recovers(gpu):
     torch.cuda.synchronize()
     assert _lib.device_status(None) == _lib.OK
     assert torch.equal(out.view(torch.int32), ref.view(torch.int32))
+
+
+def test_runner_bf16_operands_match_f32_operands(gpu, tmp_path):
+    """The runner's --operands bf16 (A and B rounded once before timing, the GEMM timed on the
+    bf16 copies) writes the same output bits as the BF16-mode call on f32 operands."""
+    import json
+    import subprocess
+
+    from tensorforge_b200 import tforge_gpu as tg
+
+    outs = {}
+    for ops in ("f32", "bf16"):
+        path = tmp_path / f"{ops}.bin"
+        r = subprocess.run([str(tg.GPU_BENCH), "--mode", "lib", "--workload", "mbr", "--m", "700", "--n", "520",
+                            "--k", "264", "--precision", "bf16", "--operands", ops, "--warmup", "1", "--reps", "2",
+                            "--seed", "71", "--out", str(path)], capture_output=True, text=True, check=True)
+        assert json.loads(r.stdout)["median_ms"] > 0
+        outs[ops] = np.fromfile(path, dtype=np.uint32)
+    assert outs["f32"].size == 700 * 520
+    assert np.array_equal(outs["f32"], outs["bf16"])
