@@ -28,7 +28,9 @@
 //                (lempty[l]) in both CTAs, a last one signals accf in both.  Peer CTA:
 //                relays its conv[o] to the leader's ready[o] with one st.async token per
 //                k-block.
-//   warps 4..11  epilogue (each CTA): its 128 rows x BN columns from its own TMEM.
+//   warps 0..11  epilogue (each CTA), once the accumulator is complete: its 128 rows x BN
+//                columns from its own TMEM, in three groups of four warps (one per TMEM
+//                lane quadrant) taking the 32-column chunks in turn.
 //
 // The split (kPairSplit): the tensor core reads an f32 operand as TF32 by dropping its low
 // 13 mantissa bits, so the truncation split keeps hi = x and computes only
@@ -85,7 +87,11 @@ struct PairLayout {
   // 3xTF32: warps 0 producer, 1 MMA (leader) / relay (peer), 2..11 converters.
   static constexpr bool kX3 = PREC == PREC_X3;
   static constexpr int kThreads = kX3 ? 384 : 256;
-  static constexpr int kEpiWarps = kX3 ? 8 : 4;         // warps 4 .. 4 + kEpiWarps - 1
+  // Epilogue warps kEpiWarp0 .. + kEpiWarps - 1.  3xTF32: all twelve -- the producer, MMA and
+  // B-only converter warps (0..3) are idle once the accumulator is complete, and three groups
+  // of four take the eight 32-column chunks in turn (at most three each).  TF32 / BF16: 4..7.
+  static constexpr int kEpiWarp0 = kX3 ? 0 : 4;
+  static constexpr int kEpiWarps = kX3 ? 12 : 4;
   static constexpr int kElem = PREC == PREC_BF16 ? 2 : 4;
   static constexpr int kBK = 128 / kElem;              // K elements per stage (one 128-B row)
   static constexpr int kUmmaK = 32 / kElem;            // K per MMA instruction
@@ -470,7 +476,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   // stores the box with TMA, which clips rows >= M and columns >= N.  The ring is free:
   // every load was consumed before accf.  matmul_add first brings its C_res boxes in the
   // same way (TMA loads into the boxes, then in-place update).
-  if (warp >= 4 && warp < 4 + L::kEpiWarps) {
+  if (warp >= L::kEpiWarp0 && warp < L::kEpiWarp0 + L::kEpiWarps) {
     // One thread waits (bounded) for the accumulator and publishes the outcome, so every
     // epilogue warp takes the same branch and the named barriers below cannot be left
     // waiting for a warp that gave up.
@@ -526,9 +532,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
       if (q == 0 && lane == 0) bulk_wait_group_read0();  // staging stays valid until read
     } else if (*epi_ok) {
       tc_fence_after();
-      constexpr int kChunksPerWarp = 8 / (L::kEpiWarps / 4);  // column chunks of 32 per warp
+      constexpr int kGroups = L::kEpiWarps / 4;  // group g takes column chunks g, g + kGroups, ...
       const int q = warp & 3;
-      const int c0 = ((warp - 4) >> 2) * kChunksPerWarp;
+      const int g = (warp - L::kEpiWarp0) >> 2;
       const int r = q * 32 + lane;  // row within this CTA's 128 rows
       const bool cta_rows = m0 < p.M;
       bool res_ok = true;
@@ -542,7 +548,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         res_ok = !cta_rows || mbar_wait_cluster(resf, 0, wc);
       }
 #pragma unroll 1
-      for (int c = c0; c < c0 + kChunksPerWarp; ++c) {
+      for (int c = g; c < 8; c += kGroups) {
         uint32_t rr[32];
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, rr);
         tmem_ld_wait(rr);

@@ -411,12 +411,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 // IEEE-2019 maximum(x, +0.0): a NaN input is returned unchanged (payload kept, as the
 // reference's fold keeps 0x7FC00000, test/Transforms/canonicalize.mlir:90-100), -0.0 and
-// negatives give +0.0.  Written on the bit pattern: a float compare-and-select may be
-// contracted into a max instruction that returns the canonical NaN instead.
+// negatives give +0.0.  One ordered compare and a select, in PTX so that it is not
+// contracted into a max instruction (which would return the canonical NaN): x <= 0 is
+// false for a NaN, which is kept, and true for -0.0, which becomes +0.0.
 __device__ __forceinline__ float relu_ieee(float x) {
-  const uint32_t u = __float_as_uint(x);
-  const bool keep = static_cast<int32_t>(u) > 0 || (u & 0x7FFFFFFFu) > 0x7F800000u;  // > +0 or NaN
-  return __uint_as_float(keep ? u : 0u);
+  float y;
+  asm("{\n\t.reg .pred p;\n\tsetp.le.f32 p, %1, 0f00000000;\n\tselp.f32 %0, 0f00000000, %1, p;\n\t}"
+      : "=f"(y)
+      : "f"(x));
+  return y;
 }
 
 // ---- 3xTF32 operand split -----------------------------------------------------------
