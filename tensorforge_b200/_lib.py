@@ -126,7 +126,8 @@ def set_config(kernel: int = 0, bn: int = 0, stages: int = 0, persistent: int = 
                b_layout: int = 0) -> None:
     """Force a kernel configuration (kernel 1 = one-CTA tcgen05, 2 = SIMT, 3 = CTA pair;
     split_k: pairs per tile for the pair kernel, 1 = none; b_layout (TF32 pair kernels):
-    1 = B as given, 2 = a transposed K-major copy); all zeros = table."""
+    1 = B as given, 2 = a transposed K-major copy, 3 = B as given in 128-byte column blocks
+    instead of k-group-major tiles); all zeros = table."""
     if kernel == 0 and bn == 0 and stages == 0 and persistent == 0 and split_k == 0 and b_layout == 0:
         check(lib().tforge_set_config(None), "tforge_set_config")
         return

@@ -99,8 +99,6 @@ struct PairLayout {
   static constexpr int kNBlk = 128 / kElem;            // N elements per 128-B MN block
   static constexpr int kBNHalf = 128;                  // B columns loaded by each CTA
   static constexpr int kBBlocks = kBNHalf / kNBlk;     // TMA boxes per B half
-  static constexpr uint32_t kBSwz = kElem == 4 ? 1u : 2u;
-  static constexpr uint32_t kBSbo = kElem == 4 ? 512u : 1024u;
   static constexpr int kABytes = 128 * 128;            // this CTA's 128 A rows
   static constexpr int kBBytes = kBNHalf * kBK * kElem;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -185,7 +183,7 @@ __device__ __forceinline__ void relay_stages(uint32_t conv0, uint32_t ready0, ui
   }
 }
 
-template <int PREC, int STAGES, int EPI, int SPLIT, int BN, bool OUTB, bool BKM>
+template <int PREC, int STAGES, int EPI, int SPLIT, int BN, bool OUTB, bool BKM, bool BAT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STAGES>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmC,
@@ -198,6 +196,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   // TF32, 256-wide tiles, B as given: operands exchanged (B's MN-major tile on the M side),
   // transposed epilogue.
   constexpr bool kSwap = PREC == PREC_TF32 && BN == 256 && kTf32Swap && !BKM;
+  // B as given (TF32, 256-wide tiles): its tile in the k-group-major tiling (BAT, one 4-D box,
+  // TcParams::b_atoms) or in column blocks.  A compile-time choice: the MMA issuer's loop is
+  // on the critical path, and selecting descriptor strides at run time measured 6-8 % slower.
+  using BT = BTileMN<L::kElem>;
+  static_assert(!BAT || (PREC == PREC_TF32 && BN == 256 && !BKM && !OUTB), "k-group-major B configuration");
+  constexpr bool b_atoms = BAT;
   constexpr uint32_t kIdesc = kSwap  ? instr_desc_a_mn(2u, 256, 256)
                               : BKM ? (instr_desc(2u, 256, 256) & ~(1u << 16))  // B K-major
                                     : instr_desc(kTF32 ? 2u : 1u, 256, BN);
@@ -319,6 +323,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         tma_load_2d_pair(sbase + L::a_off(s), &tmA, kc, m0, lead_full0 + 8 * s);
         if constexpr (BKM) {
           tma_load_2d_pair(sbase + L::b_off(s), &tmB, kc, nb, lead_full0 + 8 * s);  // 128 n-rows x 32 k
+        } else if constexpr (b_atoms) {
+          tma_load_4d_pair(sbase + L::b_off(s), &tmB, 0, 0, nb / L::kNBlk, kc / BT::kRows, lead_full0 + 8 * s);
         } else {
 #pragma unroll
           for (int j = 0; j < L::kBBlocks; ++j)
@@ -359,19 +365,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
         for (int ks = 0; ks < L::kKSteps; ++ks) {
           if constexpr (kX3) {
             const uint32_t a_hi = tmem + L::a_tmem_col(s) + 8 * ks, a_lo = a_hi + 32;
-            const uint64_t bl = smem_desc(sbase + L::lo_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
-                                          L::kBSbo, L::kBSwz);
-            const uint64_t bh = smem_desc(sbase + (kPairHiDirect ? L::b_off(land) : L::hi_off(s)) +
-                                              ks * L::kUmmaK * 128,
-                                          L::kBK * 128, L::kBSbo, L::kBSwz);
+            const uint64_t bl = BT::desc(sbase + L::lo_off(s), ks, false);
+            const uint64_t bh = BT::desc(sbase + (kPairHiDirect ? L::b_off(land) : L::hi_off(s)), ks, false);
             mma_ts_pair_tf32(tmem, a_lo, bh, kIdesc, accum);
             mma_ts_pair_tf32(tmem, a_hi, bl, kIdesc, 1u);
             mma_ts_pair_tf32(tmem, a_hi, bh, kIdesc, 1u);
           } else {
             const uint64_t ad = smem_desc(sbase + L::a_off(s) + ks * 32, 16, 1024, 2);
             const uint64_t bd = BKM ? smem_desc(sbase + L::b_off(s) + ks * 32, 16, 1024, 2)
-                                    : smem_desc(sbase + L::b_off(s) + ks * L::kUmmaK * 128, L::kBK * 128,
-                                                L::kBSbo, L::kBSwz);
+                                    : BT::desc(sbase + L::b_off(s), ks, b_atoms);
             if constexpr (kSwap)
               mma_ss_pair<kTF32>(tmem, bd, ad, kIdesc, accum);
             else
@@ -643,11 +645,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   }
 }
 
-template <int PREC, int STAGES, int EPI, int BN, bool OUTB, bool BKM = false>
+template <int PREC, int STAGES, int EPI, int BN, bool OUTB, bool BKM = false, bool BAT = false>
 cudaError_t launch_pair_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
                              const CUtensorMap &tmC, const TcParams &p, cudaStream_t stream) {
   using L = PairLayout<PREC, STAGES>;
-  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit, BN, OUTB, BKM>;
+  auto kern = gemm_pair_kernel<PREC, STAGES, EPI, kPairSplit, BN, OUTB, BKM, BAT>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -685,6 +687,11 @@ cudaError_t launch_pair_one(const CUtensorMap &tmA, const CUtensorMap &tmB, cons
                           : launch_pair_kern<PREC, STAGES, EPI, BN, true>(tmA, tmB, tmO, tmC, p, stream);
     return cudaErrorInvalidValue;
   }
+  if (p.b_atoms) {
+    if constexpr (PREC == PREC_TF32 && BN == 256)
+      return launch_pair_kern<PREC, STAGES, EPI, BN, false, false, true>(tmA, tmB, tmO, tmC, p, stream);
+    return cudaErrorInvalidValue;
+  }
   return launch_pair_kern<PREC, STAGES, EPI, BN, false>(tmA, tmB, tmO, tmC, p, stream);
 }
 
@@ -702,9 +709,9 @@ cudaError_t launch_pair_epi(int epi, const CUtensorMap &tmA, const CUtensorMap &
 template <int PREC, int STAGES, int BN>
 cudaError_t pair_attrs(int epi, cudaFuncAttributes *a, int *blocks) {
   using L = PairLayout<PREC, STAGES>;
-  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit, BN, false, false>)
-                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit, BN, false, false>)
-                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit, BN, false, false>);
+  const void *f = epi == EPI_MBR   ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MBR, kPairSplit, BN, false, false, false>)
+                  : epi == EPI_ADD ? reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_ADD, kPairSplit, BN, false, false, false>)
+                                   : reinterpret_cast<const void *>(gemm_pair_kernel<PREC, STAGES, EPI_MATMUL, kPairSplit, BN, false, false, false>);
   cudaError_t e = cudaFuncGetAttributes(a, f);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);

@@ -54,8 +54,6 @@ struct PersistLayout {
   static constexpr int kKSteps = kBK / kUmmaK;      // 4
   static constexpr int kNBlk = 128 / kElem;         // B columns per 128-B MN block
   static constexpr int kBBlocks = 128 / kNBlk;      // TMA boxes per B half
-  static constexpr uint32_t kBSwz = kElem == 4 ? 1u : 2u;
-  static constexpr uint32_t kBSbo = kElem == 4 ? 512u : 1024u;
   static constexpr int kABytes = 128 * 128;         // this CTA's 128 A rows
   static constexpr int kBBytes = 128 * kBK * kElem;  // this CTA's 128 B columns
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -77,7 +75,7 @@ __device__ __forceinline__ void pause_ns(uint64_t ns) {
   while (globaltimer() - t0 < ns) __nanosleep(1000);
 }
 
-template <int PREC, int STAGES, int EPI, bool OUTB, bool BKM>
+template <int PREC, int STAGES, int EPI, bool OUTB, bool BKM, bool BAT = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 const __grid_constant__ CUtensorMap tmO, const TcParams p) {
@@ -92,6 +90,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   // bf16 output (OUTB): BF16 precision and the mbr epilogue only.
   static_assert(!OUTB || (PREC == PREC_BF16 && EPI == EPI_MBR), "bf16 output configuration");
   static_assert(!BKM || PREC == PREC_TF32, "K-major B configuration");
+  // B as given (TF32): its tile in the k-group-major tiling (BAT, one 4-D box,
+  // TcParams::b_atoms) or in column blocks; a compile-time choice, as in gemm_pair_kernel.
+  using BT = BTileMN<L::kElem>;
+  static_assert(!BAT || (kTF32 && !BKM && !OUTB), "k-group-major B configuration");
+  constexpr bool b_atoms = BAT;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -169,6 +172,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         tma_load_2d_pair(slot, &tmA, kc, m0, lead_full0 + 8 * s);
         if constexpr (BKM) {
           tma_load_2d_pair(slot + L::kABytes, &tmB, kc, nb, lead_full0 + 8 * s);  // 128 n-rows x 32 k
+        } else if constexpr (b_atoms) {
+          tma_load_4d_pair(slot + L::kABytes, &tmB, 0, 0, nb / L::kNBlk, kc / BT::kRows, lead_full0 + 8 * s);
         } else {
 #pragma unroll
           for (int j = 0; j < L::kBBlocks; ++j)
@@ -211,7 +216,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         for (int ks = 0; ks < L::kKSteps; ++ks) {
           const uint64_t ad = smem_desc(slot + ks * 32, 16, 1024, 2);
           const uint64_t bd = BKM ? smem_desc(slot + L::kABytes + ks * 32, 16, 1024, 2)
-                                  : smem_desc(slot + L::kABytes + ks * L::kUmmaK * 128, L::kBK * 128, L::kBSbo, L::kBSwz);
+                                  : BT::desc(slot + L::kABytes, ks, b_atoms);
           if constexpr (kSwap)
             mma_ss_pair<kTF32>(acc, bd, ad, kIdesc, (kb | ks) ? 1u : 0u);
           else
@@ -378,10 +383,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 }
 
 // Co-resident clusters of one instantiation on the current device (0 on failure).
-template <int PREC, int STAGES, int EPI, bool OUTB = false, bool BKM = false>
+template <int PREC, int STAGES, int EPI, bool OUTB = false, bool BKM = false, bool BAT = false>
 int persist_clusters() {
   using L = PersistLayout<PREC, STAGES>;
-  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM>;
+  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM, BAT>;
   static int cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -416,15 +421,15 @@ int persist_clusters() {
   return n;
 }
 
-template <int PREC, int STAGES, int EPI, bool OUTB, bool BKM = false>
+template <int PREC, int STAGES, int EPI, bool OUTB, bool BKM = false, bool BAT = false>
 cudaError_t launch_persist_kern(const CUtensorMap &tmA, const CUtensorMap &tmB, const CUtensorMap &tmO,
                                 const TcParams &p, cudaStream_t stream) {
   using L = PersistLayout<PREC, STAGES>;
-  const int clusters = persist_clusters<PREC, STAGES, EPI, OUTB, BKM>();
+  const int clusters = persist_clusters<PREC, STAGES, EPI, OUTB, BKM, BAT>();
   if (clusters <= 0) return cudaErrorInvalidConfiguration;
   const int64_t tiles = (int64_t)((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int pairs = tiles < clusters ? (int)tiles : clusters;
-  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM>;
+  auto kern = gemm_pair_persistent_kernel<PREC, STAGES, EPI, OUTB, BKM, BAT>;
   if (p.pdl) {
     cudaLaunchAttribute attr[1];
     pdl_attr(attr[0]);
@@ -447,6 +452,10 @@ cudaError_t launch_persist_one(const CUtensorMap &tmA, const CUtensorMap &tmB, c
   if (p.out_bf16) {
     if constexpr (PREC == PREC_BF16 && EPI == EPI_MBR)
       return launch_persist_kern<PREC, STAGES, EPI, true>(tmA, tmB, tmO, p, stream);
+    return cudaErrorInvalidValue;
+  }
+  if (p.b_atoms) {
+    if constexpr (PREC == PREC_TF32) return launch_persist_kern<PREC, STAGES, EPI, false, false, true>(tmA, tmB, tmO, p, stream);
     return cudaErrorInvalidValue;
   }
   return launch_persist_kern<PREC, STAGES, EPI, false>(tmA, tmB, tmO, p, stream);

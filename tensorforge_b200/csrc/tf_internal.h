@@ -53,6 +53,10 @@ struct TcParams {
   // 1 (TF32, 256-wide pair tiles or the persistent pair kernel): tmB maps a transposed copy
   // of B (N x K, K-major tiles of 128 columns x 32 k); the MMAs read both operands K-major.
   int32_t b_kmajor;
+  // 1 (TF32, B as given, 256-wide pair tiles or the persistent pair kernel, N a multiple of 32
+  // and K of 4): tmB is the 4-D map of the k-group-major B tiling (BTileMN, tf_ptx.cuh) and the
+  // kernel instantiation reads that tiling; 0: the 2-D map of 128-B column blocks.
+  int32_t b_atoms;
   // 1: the launch is a programmatic dependent of the kernel just before it on the stream (the
   // operand conversion or B transpose that wrote what tmA / tmB read): the CTAs set up while
   // that kernel finishes, and the TMA producer waits for it (griddepcontrol.wait) before its

@@ -123,6 +123,24 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *tmap,
       : "memory");
 }
 
+// 4-D tiled loads (the k-group-major B tile, b_mn_desc); same completion as the 2-D forms.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *tmap, int32_t c0, int32_t c1, int32_t c2,
+                                            int32_t c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void *tmap, int32_t c0, int32_t c1, int32_t c2,
+                                                 int32_t c3, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar_cluster)
+      : "memory");
+}
+
 // 2-D tiled store shared -> global (bulk-group completion); TMA clips rows and columns
 // outside the tensor.  Coordinates must be non-negative.
 __device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int32_t c0, int32_t c1) {
@@ -388,6 +406,30 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)swizzle << 61);
 }
+
+// One CTA's MN-major B tile: 128 columns x (128 / ELEM) k-rows, ELEM-byte elements, 128-B
+// swizzle (TF32: the 32-B-atom form).  The swizzle atom is 128 B of columns x kRows k-rows
+// (TF32 32 columns x 4 rows = 512 B, BF16 64 x 8 = 1 KB).  Two tilings of those atoms:
+//   column blocks (atoms = false): each 128-B column block holds all of the tile's k-rows,
+//     atoms along K one atom apart, blocks (128 / ELEM) x 128 B apart -- one 2-D TMA box per
+//     block;
+//   k-group major (atoms = true): the column blocks' atoms of one k-group sit side by side
+//     (one atom apart), k-groups (128 / (128 / ELEM)) atoms apart -- one 4-D TMA box
+//     (columns in block, rows in group, blocks, groups) per tile.
+// Same bytes, same results; the tensor core reads the k-group-major tiling faster (TF32 mbr
+// 4096^3 671 -> 763 TFLOP/s on the persistent pair kernel).  The descriptor's leading byte
+// offset is the stride between column blocks, its stride byte offset that between k-groups.
+template <int ELEM>
+struct BTileMN {
+  static constexpr int kBK = 128 / ELEM, kUmmaK = 32 / ELEM, kNBlk = 128 / ELEM, kBlocks = 128 / kNBlk;
+  static constexpr int kRows = ELEM == 4 ? 4 : 8;  // k-rows per atom
+  static constexpr uint32_t kAtom = kRows * 128, kSwz = ELEM == 4 ? 1u : 2u;
+  // Descriptor of k-step ks (kUmmaK k-rows) of the tile at `tile`.
+  __device__ __forceinline__ static uint64_t desc(uint32_t tile, int ks, bool atoms) {
+    return atoms ? smem_desc(tile + ks * (kUmmaK / kRows) * kBlocks * kAtom, kAtom, kBlocks * kAtom, kSwz)
+                 : smem_desc(tile + ks * kUmmaK * 128, kBK * 128, kAtom, kSwz);
+  }
+};
 
 // Instruction descriptor for kind::tf32 / kind::f16: D f32 (bit 4), A/B format in [7,10)
 // and [10,13) (1 = bf16, 2 = tf32), A K-major (bit 15 = 0), B MN-major (bit 16 = 1),

@@ -181,8 +181,9 @@ def test_forced_config_and_reset():
         _lib.set_config(3, 0, 0, 1, 2)  # no split-K either
         with pytest.raises(_lib.TforgeError):
             _lib.describe("mbr", 8192, 8192, 8192, "tf32")
-        with pytest.raises(_lib.TforgeError):  # b_layout is 0, 1 or 2
-            _lib.set_config(3, 0, 0, 0, 0, 3)
+        _lib.set_config(3, 0, 0, 0, 0, 3)  # b_layout is 0 .. 3
+        with pytest.raises(_lib.TforgeError):
+            _lib.set_config(3, 0, 0, 0, 0, 4)
     finally:
         _lib.set_config()
     assert _lib.describe("mbr", 2048, 2048, 2048, "tf32")["kernel"] == "tf_gemm_tcgen05_tf32_pair"

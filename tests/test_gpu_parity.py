@@ -561,6 +561,31 @@ def test_tf32_transposed_b_within_bound_and_bitwise(gpu, workload, cfg, shape):
     assert np.array_equal(bits(outs[0]), bits(outs[1]))
 
 
+@pytest.mark.parametrize("workload", ["mbr", "matmul", "matmul_add"])
+@pytest.mark.parametrize("cfg", [(3, 256, 0, 0, 1), (3, 0, 0, 1, 0), (3, 256, 0, 0, 3)],
+                         ids=["pair", "persistent", "pair-split3"])
+@pytest.mark.parametrize("shape", [(700, 2080, 520), (2600, 1024, 264), (300, 4096, 1028)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_tf32_b_tile_layouts_bitwise(gpu, workload, cfg, shape):
+    """TF32, B as given, loaded as k-group-major tiles (the default where N and K allow it, one
+    4-D box per tile) or in 128-byte column blocks (b_layout = 3): the tensor core reads the
+    same values in the same order, so the results are the same bits, and within the TF32
+    bound; ragged M, N a multiple of 32 but not of the tile width, K tails, every epilogue,
+    split-K."""
+    m, n, k = shape
+    ins = tc.make_inputs(workload, m, n, k, 53)
+    outs = []
+    for layout in (1, 3):
+        _lib.set_config(*cfg, b_layout=layout)
+        try:
+            outs.append(tg.run_op(workload, ins, m, n, k, "tf32"))
+        finally:
+            _lib.set_config()
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    res = tc.check_output(workload, ins, outs[0], "tf32")
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+
+
 def _bf16_rne_bits(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even f32 -> bf16 bit patterns (NaNs left to the caller)."""
     u = x.view(np.uint32).astype(np.uint64)
