@@ -349,40 +349,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<PREC, STA
   } else if (warp == 1 && lane == 0) {
     if (rank == 0) {
       // ---------------- pair MMA issuer (leader CTA) ----------------
-      uint32_t accum = 0;
+      // This thread's loop is on the critical path: ring positions are kept incrementally
+      // (slot s of kO with phase ph; 3xTF32 landing slot land of kL) and the descriptors are the
+      // slot-0 ones plus constant offsets in 16-B units.
+      uint32_t accum = 0, ph = 0;
+      int s = 0, land = 0;
+      uint32_t s_off = 0, land_off = 0;  // 16-B units: slot s, landing slot land
+      constexpr uint32_t kSlot16 = (kX3 ? L::kOpBytes : L::kStageBytes) >> 4, kLand16 = L::kStageBytes >> 4;
+      constexpr uint32_t kBStep = BKM ? 2u : BT::step(b_atoms) >> 4;
+      const uint64_t a_d0 = smem_desc(sbase + L::a_off(0), 16, 1024, 2);
+      const uint64_t b_d0 = BKM ? smem_desc(sbase + L::b_off(0), 16, 1024, 2) : BT::desc(sbase + L::b_off(0), 0, b_atoms);
+      const uint64_t lo_d0 = BT::desc(sbase + L::lo_off(0), 0, false);  // 3xTF32 B lo (operand slot)
+      const uint64_t hi_d0 = BT::desc(sbase + (kPairHiDirect ? L::b_off(0) : L::hi_off(0)), 0, false);
       for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kO, round = kb / kO;
         if constexpr (kX3) {
-          if (!mbar_wait(conv0 + 8 * s, round & 1, wc)) break;
+          if (!mbar_wait(conv0 + 8 * s, ph, wc)) break;
           mbar_arrive_expect_tx(ready0 + 8 * s, 4);  // the peer's token for this round
-          if (!mbar_wait_cluster(ready0 + 8 * s, round & 1, wc)) break;
+          if (!mbar_wait_cluster(ready0 + 8 * s, ph, wc)) break;
         } else {
-          if (!mbar_wait_cluster(full0 + 8 * s, round & 1, wc)) break;
+          if (!mbar_wait_cluster(full0 + 8 * s, ph, wc)) break;
         }
         tc_fence_after();
-        const int land = kb % kL;  // 3xTF32: landing slot holding this k-block's raw B (= B hi)
+        // 3xTF32: landing slot `land` holds this k-block's raw B (= B hi).
+        const uint64_t bl = lo_d0 + s_off, bh = hi_d0 + (kPairHiDirect ? land_off : s_off);
+        const uint64_t ad = a_d0 + s_off, bd = b_d0 + s_off;
+        const uint32_t a_hi0 = tmem + L::a_tmem_col(s);
 #pragma unroll
         for (int ks = 0; ks < L::kKSteps; ++ks) {
           if constexpr (kX3) {
-            const uint32_t a_hi = tmem + L::a_tmem_col(s) + 8 * ks, a_lo = a_hi + 32;
-            const uint64_t bl = BT::desc(sbase + L::lo_off(s), ks, false);
-            const uint64_t bh = BT::desc(sbase + (kPairHiDirect ? L::b_off(land) : L::hi_off(s)), ks, false);
-            mma_ts_pair_tf32(tmem, a_lo, bh, kIdesc, accum);
-            mma_ts_pair_tf32(tmem, a_hi, bl, kIdesc, 1u);
-            mma_ts_pair_tf32(tmem, a_hi, bh, kIdesc, 1u);
+            const uint32_t a_hi = a_hi0 + 8 * ks, a_lo = a_hi + 32;
+            mma_ts_pair_tf32(tmem, a_lo, bh + ks * kBStep, kIdesc, accum);
+            mma_ts_pair_tf32(tmem, a_hi, bl + ks * kBStep, kIdesc, 1u);
+            mma_ts_pair_tf32(tmem, a_hi, bh + ks * kBStep, kIdesc, 1u);
           } else {
-            const uint64_t ad = smem_desc(sbase + L::a_off(s) + ks * 32, 16, 1024, 2);
-            const uint64_t bd = BKM ? smem_desc(sbase + L::b_off(s) + ks * 32, 16, 1024, 2)
-                                    : BT::desc(sbase + L::b_off(s), ks, b_atoms);
             if constexpr (kSwap)
-              mma_ss_pair<kTF32>(tmem, bd, ad, kIdesc, accum);
+              mma_ss_pair<kTF32>(tmem, bd + ks * kBStep, ad + 2 * ks, kIdesc, accum);
             else
-              mma_ss_pair<kTF32>(tmem, ad, bd, kIdesc, accum);
+              mma_ss_pair<kTF32>(tmem, ad + 2 * ks, bd + ks * kBStep, kIdesc, accum);
           }
           accum = 1u;
         }
         mma_commit_pair(empty0 + 8 * s, 0x3);
         if constexpr (kX3 && kPairHiDirect) mma_commit_pair(lempty0 + 8 * land, 0x3);
+        if (++s == kO) {
+          s = 0;
+          s_off = 0;
+          ph ^= 1u;
+        } else {
+          s_off += kSlot16;
+        }
+        if constexpr (kX3) {
+          if (++land == kL) {
+            land = 0;
+            land_off = 0;
+          } else {
+            land_off += kLand16;
+          }
+        }
       }
       mma_commit_pair(accf, 0x3);
       if (*abort_flag) mbar_wait_drain_cluster(accf, 0, p.limit_ns);

@@ -196,33 +196,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------- pair MMA issuer (leader CTA) ----------------
-    int g = 0;
+    // Ring slot s and its phase are kept incrementally, and the descriptors are the slot-0 ones
+    // plus constant offsets (16-B units): this thread's loop is on the critical path.
     bool ok = true;
+    const uint64_t a_d0 = smem_desc(sbase, 16, 1024, 2);
+    const uint64_t b_d0 = BKM ? smem_desc(sbase + L::kABytes, 16, 1024, 2) : BT::desc(sbase + L::kABytes, 0, b_atoms);
+    constexpr uint32_t kBStep = BKM ? 2u : BT::step(b_atoms) >> 4;
+    int s = 0;
+    uint32_t phase = 0, bar = full0;
+    uint64_t so = 0;
     for (int i = 0; i < my_tiles && ok; ++i) {
       const int b = i & 1;
       const uint32_t acc = tmem + 256u * b;
       // Use u = i / 2 of accumulator b needs the epilogues' release of use u - 1.
       if (i >= 2 && !mbar_wait_cluster(acce0 + 8 * b, ((i >> 1) - 1) & 1, wc)) break;
       tc_fence_after();
-      for (int kb = 0; kb < nkb; ++kb, ++g) {
-        const int s = g % STAGES, round = g / STAGES;
-        if (!mbar_wait_cluster(full0 + 8 * s, round & 1, wc)) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait_cluster(bar, phase, wc)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t slot = sbase + s * L::kStageBytes;
+        const uint64_t ad = a_d0 + so, bd = b_d0 + so;
 #pragma unroll
         for (int ks = 0; ks < L::kKSteps; ++ks) {
-          const uint64_t ad = smem_desc(slot + ks * 32, 16, 1024, 2);
-          const uint64_t bd = BKM ? smem_desc(slot + L::kABytes + ks * 32, 16, 1024, 2)
-                                  : BT::desc(slot + L::kABytes, ks, b_atoms);
           if constexpr (kSwap)
-            mma_ss_pair<kTF32>(acc, bd, ad, kIdesc, (kb | ks) ? 1u : 0u);
+            mma_ss_pair<kTF32>(acc, bd + ks * kBStep, ad + 2 * ks, kIdesc, (kb | ks) ? 1u : 0u);
           else
-            mma_ss_pair<kTF32>(acc, ad, bd, kIdesc, (kb | ks) ? 1u : 0u);
+            mma_ss_pair<kTF32>(acc, ad + 2 * ks, bd + ks * kBStep, kIdesc, (kb | ks) ? 1u : 0u);
         }
-        mma_commit_pair(empty0 + 8 * s, 0x3);
+        mma_commit_pair(bar + 8 * STAGES, 0x3);
+        if (++s == STAGES) {
+          s = 0;
+          phase ^= 1u;
+          bar = full0;
+          so = 0;
+        } else {
+          bar += 8;
+          so += L::kStageBytes >> 4;
+        }
       }
       if (!ok) break;
       mma_commit_pair(accf0 + 8 * b, 0x3);

@@ -424,10 +424,14 @@ struct BTileMN {
   static constexpr int kBK = 128 / ELEM, kUmmaK = 32 / ELEM, kNBlk = 128 / ELEM, kBlocks = 128 / kNBlk;
   static constexpr int kRows = ELEM == 4 ? 4 : 8;  // k-rows per atom
   static constexpr uint32_t kAtom = kRows * 128, kSwz = ELEM == 4 ? 1u : 2u;
-  // Descriptor of k-step ks (kUmmaK k-rows) of the tile at `tile`.
+  // Bytes between k-steps (kUmmaK k-rows).
+  __host__ __device__ static constexpr uint32_t step(bool atoms) {
+    return atoms ? (kUmmaK / kRows) * kBlocks * kAtom : kUmmaK * 128;
+  }
+  // Descriptor of k-step ks of the tile at `tile`.
   __device__ __forceinline__ static uint64_t desc(uint32_t tile, int ks, bool atoms) {
-    return atoms ? smem_desc(tile + ks * (kUmmaK / kRows) * kBlocks * kAtom, kAtom, kBlocks * kAtom, kSwz)
-                 : smem_desc(tile + ks * kUmmaK * 128, kBK * 128, kAtom, kSwz);
+    return atoms ? smem_desc(tile + ks * step(true), kAtom, kBlocks * kAtom, kSwz)
+                 : smem_desc(tile + ks * step(false), kBK * 128, kAtom, kSwz);
   }
 };
 
