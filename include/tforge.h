@@ -170,12 +170,11 @@ typedef struct tforge_config {
                             256x256 tiles, two TMEM accumulators, no split-K) */
   int32_t split_k;       /* CTA-pair kernel in fp32 / TF32 mode: 0 = automatic, 1 = no split,
                             S = 2..8 pairs per tile, each over K / S */
-  int32_t b_layout;      /* TF32 mode, 256-wide pair and persistent pair kernels: 0 = automatic
-                            (a transposed, K-major copy of B when M >= 16384 and K >= 4096), 1 = B
-                            as given, 2 = always the transposed copy, 3 = B as given in 128-byte
-                            column blocks.  B as given is otherwise loaded as k-group-major tiles
-                            (one 4-D box per tile) when N is a multiple of 32 and K of 4.  Every
-                            form gives the same bits. */
+  int32_t b_layout;      /* TF32 mode, 256-wide pair and persistent pair kernels: 0 or 1 = B as
+                            given, loaded as k-group-major tiles (one 4-D box per tile) when N is
+                            a multiple of 32 and K of 4, else in 128-byte column blocks; 2 = a
+                            transposed, K-major copy of B (one extra pass over B); 3 = B as given
+                            in column blocks.  Every form gives the same bits. */
 } tforge_config;
 
 int tforge_set_config(const tforge_config *cfg);

@@ -447,11 +447,11 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   const int epi = a->workload == TFORGE_MBR ? EPI_MBR : (a->workload == TFORGE_MATMUL_ADD ? EPI_ADD : EPI_MATMUL);
   cudaError_t e;
   const int splits = pair_splits(cfg, a->M, a->N, a->K);
-  // TF32 with many rows: the MMAs read a transposed (K-major) copy of B, which the tensor
-  // core takes faster than the row-major (MN-major) original; the transpose is one pass over
-  // B, amortised over M.  Measured (interleaved, same box): 16384 x 8192 x 8192 +3 to +10 %,
-  // 65536 x 8192 x 8192 +2 to +6 %; 8192^3 even; 4096^3 and 8192 x 4096 x 1024 slower (short
-  // K loops gain less from the K-major read), hence M >= 16384 and K >= 4096.
+  // TF32, b_layout = 2 only: the MMAs read a transposed (K-major) copy of B made by one pass
+  // over B.  It used to be the default from M = 16384 rows, when B as given was read in column
+  // blocks; read as k-group-major tiles, B as given is as fast or faster at every size measured
+  // (16384 x 8192 x 8192 618.5 vs 576.9 TFLOP/s, 16384 x 16384 x 4096 638.1 vs 602.3,
+  // 32768 x 8192 x 8192 even; same box, interleaved) and needs no scratch.
   int b_layout = 0;
   {
     std::lock_guard<std::mutex> lk(g_cfg_mu);
@@ -459,7 +459,7 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   }
   bool bkm = !bf16 && cfg.prec == PREC_TF32 && ((cfg.pair && cfg.bn == 256) || cfg.persist) && a->K % 4 == 0 &&
              a->K <= 65535 * 32 &&  // the transpose kernel's grid
-             (b_layout == 2 || (b_layout == 0 && a->M >= 16384 && a->K >= 4096));
+             b_layout == 2;
   void *bt = nullptr;
   if (bkm) {
     cudaMemPool_t pool = nullptr;

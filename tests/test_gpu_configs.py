@@ -8,9 +8,9 @@ the stated input-rounding term (2u + u^2)|A||B| for TF32 (u = 2^-10) and BF16 (u
 * config 3: 4096^3, 8192x4096x1024 and 256x16384x4096, U[-1, 1], matmul / mbr /
   matmul_add in the fp32-accurate (3xTF32) mode; 256x16384x4096 takes 256x240 pair tiles.
 * config 4: the per-GPU shard of the M-sharded problem at 8 GPUs, 16384x8192x8192, with
-  A, B ~ N(0, 1/sqrt(K)) and bias ~ N(0, 0.1), in TF32 and BF16.  TF32 at this size reads
-  B from a transposed (K-major) copy by default; that result must equal reading B as
-  given bit for bit.
+  A, B ~ N(0, 1/sqrt(K)) and bias ~ N(0, 0.1), in TF32 and BF16.  TF32 reads B as given, in
+  k-group-major tiles; that result must equal reading a transposed (K-major) copy of B
+  bit for bit.
 * config 5: the two-layer MLP at its full widths, D = 4096 and H = 16384, with 2048 rows,
   Xavier-uniform weights and N(0, 0.02) biases, each layer checked against its own FP64
   reference (layer 2 on the kernel's own H), fp32 and BF16 with a bf16 H.
@@ -74,15 +74,15 @@ def test_config4_shard_tf32_transposed_b_bitwise_and_bound(gpu, config4_shard):
     (m, n, k), ins, t = config4_shard
     d = _lib.describe("mbr", m, n, k, "tf32")
     assert d["kernel"].startswith("tf_gemm_tcgen05_tf32_pair")
-    auto = _mbr_device(t, m, n, k, "tf32")        # dispatch: B transposed to K-major first
-    _lib.set_config(b_layout=1)                    # the same kernel reading B as given
+    auto = _mbr_device(t, m, n, k, "tf32")        # dispatch: B as given, k-group-major tiles
+    _lib.set_config(b_layout=2)                    # the same kernel on a transposed copy of B
     try:
-        given = _mbr_device(t, m, n, k, "tf32")
+        tcopy = _mbr_device(t, m, n, k, "tf32")
     finally:
         _lib.set_config()
     import torch
 
-    assert torch.equal(auto.view(torch.int32), given.view(torch.int32))
+    assert torch.equal(auto.view(torch.int32), tcopy.view(torch.int32))
     rows = _rows(m, 41)
     o = auto[torch.from_numpy(rows).to(auto.device)].cpu().numpy()
     res = tc.check_output("mbr", {"a": ins["a"][rows], "b": ins["b"], "bias": ins["bias"]}, o, "tf32")
