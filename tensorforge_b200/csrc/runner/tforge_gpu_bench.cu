@@ -11,11 +11,13 @@
 //     --operands bf16 (BF16 precision): A and B rounded to bf16 once before timing and passed
 //     as bf16 (tforge_gemm, a_dtype = b_dtype = TFORGE_BF16), so only the GEMM is timed.
 //   tforge-gpu-bench --mode cublas --workload mbr --m M --n N --k K
-//       [--math default|tf32|bf16|bf16x9|lt|lt_tf32]
+//       [--math default|tf32|bf16|bf16x9|lt|lt_tf32|lt_bf16]
 //     default: cublasSgemm (FP32 FMA) + separate bias/relu -- the reference's comparator;
 //     tf32 / bf16: TF32 tensor-op math / bf16 inputs with f32 accumulation;
 //     bf16x9: FP32 emulated on bf16 tensor cores (CUBLAS_COMPUTE_32F_EMULATED_16BFX9, eager);
-//     lt / lt_tf32: cuBLASLt FP32 / TF32 with the bias + relu fused into its epilogue.
+//     lt / lt_tf32: cuBLASLt FP32 / TF32 with the bias + relu fused into its epilogue;
+//     lt_bf16: cuBLASLt on bf16 copies of A and B made once before timing (f32 accumulate and
+//     output, fused bias + relu) -- the counterpart of `--mode lib --precision bf16 --operands bf16`.
 //   tforge-gpu-bench ... --info-only        (launch description and occupancy, no run)
 //
 // Buffers follow the host entry's argument order (runners/gpu/tforge-gpu-bench.cu:20-24):
@@ -353,10 +355,18 @@ int main(int argc, char **argv) {
     } else if (a.math == "bf16x9") {
       blas_ok(cublasSetEmulationStrategy(blas, CUBLAS_EMULATION_STRATEGY_EAGER), "cublasSetEmulationStrategy");
       kernel = "cublasGemmEx(f32, COMPUTE_32F_EMULATED_16BFX9)";
-    } else if (a.math == "lt" || a.math == "lt_tf32") {
+    } else if (a.math == "lt" || a.math == "lt_tf32" || a.math == "lt_bf16") {
       if (wl == TFORGE_MATMUL_ADD) die("--math lt* covers matmul and mbr");
       blas_ok(cublasLtCreate(&lt), "cublasLtCreate");
-      const cublasComputeType_t ct = a.math == "lt" ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_FAST_TF32;
+      const bool ltb = a.math == "lt_bf16";
+      if (ltb) {
+        cuda_ok(cudaMalloc(&abf, M * K * 2), "cudaMalloc");
+        cuda_ok(cudaMalloc(&bbf, K * N * 2), "cudaMalloc");
+        to_bf16<<<(unsigned)((M * K + 255) / 256), 256, 0, stream>>>(dA, abf, M * K);
+        to_bf16<<<(unsigned)((K * N + 255) / 256), 256, 0, stream>>>(dB, bbf, K * N);
+        cuda_ok(cudaStreamSynchronize(stream), "bf16 copies");
+      }
+      const cublasComputeType_t ct = a.math == "lt_tf32" ? CUBLAS_COMPUTE_32F_FAST_TF32 : CUBLAS_COMPUTE_32F;
       blas_ok(cublasLtMatmulDescCreate(&ltDesc, ct, CUDA_R_32F), "cublasLtMatmulDescCreate");
       const cublasOperation_t opN = CUBLAS_OP_N;
       blas_ok(cublasLtMatmulDescSetAttribute(ltDesc, CUBLASLT_MATMUL_DESC_TRANSA, &opN, sizeof(opN)), "TRANSA");
@@ -368,8 +378,8 @@ int main(int argc, char **argv) {
         blas_ok(cublasLtMatmulDescSetAttribute(ltDesc, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &dBias, sizeof(dBias)),
                 "BIAS_POINTER");
       }
-      blas_ok(cublasLtMatrixLayoutCreate(&ltB, CUDA_R_32F, N, K, N), "layout B");
-      blas_ok(cublasLtMatrixLayoutCreate(&ltA, CUDA_R_32F, K, M, K), "layout A");
+      blas_ok(cublasLtMatrixLayoutCreate(&ltB, ltb ? CUDA_R_16BF : CUDA_R_32F, N, K, N), "layout B");
+      blas_ok(cublasLtMatrixLayoutCreate(&ltA, ltb ? CUDA_R_16BF : CUDA_R_32F, K, M, K), "layout A");
       blas_ok(cublasLtMatrixLayoutCreate(&ltC, CUDA_R_32F, N, M, N), "layout C");
       cublasLtMatmulPreference_t pref;
       blas_ok(cublasLtMatmulPreferenceCreate(&pref), "pref");
@@ -382,14 +392,16 @@ int main(int argc, char **argv) {
       blas_ok(cublasLtMatmulAlgoGetHeuristic(lt, ltDesc, ltB, ltA, ltC, ltC, pref, 1, &ltHeur, &found), "heuristic");
       if (!found) die("cuBLASLt: no algorithm");
       cublasLtMatmulPreferenceDestroy(pref);
-      kernel = a.math == "lt" ? "cublasLtMatmul(f32, RELU_BIAS epilogue)" : "cublasLtMatmul(tf32, RELU_BIAS epilogue)";
-      if (wl == TFORGE_MATMUL) kernel = a.math == "lt" ? "cublasLtMatmul(f32)" : "cublasLtMatmul(tf32)";
+      const char *prec = a.math == "lt" ? "f32" : a.math == "lt_tf32" ? "tf32" : "bf16 operands";
+      kernel = std::string("cublasLtMatmul(") + prec + (wl == TFORGE_MBR ? ", RELU_BIAS epilogue)" : ")");
     } else {
-      die("--math default|tf32|bf16|bf16x9|lt|lt_tf32");
+      die("--math default|tf32|bf16|bf16x9|lt|lt_tf32|lt_bf16");
     }
     run = [&, one, zero] {
-      if (a.math == "lt" || a.math == "lt_tf32") {
-        blas_ok(cublasLtMatmul(lt, ltDesc, &one, dB, ltB, dA, ltA, &zero, dC, ltC, dC, ltC, &ltHeur.algo, ltWs,
+      if (a.math == "lt" || a.math == "lt_tf32" || a.math == "lt_bf16") {
+        const void *lb = a.math == "lt_bf16" ? static_cast<const void *>(bbf) : dB;
+        const void *la = a.math == "lt_bf16" ? static_cast<const void *>(abf) : dA;
+        blas_ok(cublasLtMatmul(lt, ltDesc, &one, lb, ltB, la, ltA, &zero, dC, ltC, dC, ltC, &ltHeur.algo, ltWs,
                                size_t(64) << 20, stream),
                 "cublasLtMatmul");
         if (wl == TFORGE_MATMUL_ADD) add_inplace<<<(unsigned)((M * N + 255) / 256), 256, 0, stream>>>(dC, dRes, M * N);

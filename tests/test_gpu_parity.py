@@ -264,7 +264,8 @@ def test_automatic_split_k_small_square(gpu):
 
 
 @pytest.mark.parametrize("math,precision", [("default", "fp32"), ("bf16x9", "fp32"), ("lt", "fp32"),
-                                            ("lt_tf32", "tf32"), ("tf32", "tf32"), ("bf16", "bf16")])
+                                            ("lt_tf32", "tf32"), ("tf32", "tf32"), ("bf16", "bf16"),
+                                            ("lt_bf16", "bf16")])
 def test_runner_cublas_comparators_within_bound(gpu, tmp_path, math, precision):
     """Every cuBLAS comparator path of the runner computes relu(A@B+bias) on the reference's
     inputs within the bound of its precision (bf16x9 emulation and FP32 paths: the fp32
