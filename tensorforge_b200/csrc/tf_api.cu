@@ -87,27 +87,24 @@ int make_tmap(CUtensorMap *m, const void *base, bool bf16, int64_t rows, int64_t
   return TFORGE_OK;
 }
 
-// B (K x N, row pitch ldb elements) as a 4-D map whose box is one CTA's 128-column B tile in
-// the k-group-major tiling of BTileMN (tf_ptx.cuh): dims (columns in a 128-B block, rows in a
-// k-group, column blocks, k-groups) with byte strides (-, ldb, 128, rows x ldb); the box is one
-// block wide, one group high, the tile's blocks and a stage's groups deep.  Needs N a multiple
-// of the block width and K of the group height, so that no element of a box lies outside B
-// (the per-dimension bounds cannot see a partial block or group); k-groups past K read as zero.
-int make_tmap_b_atoms(CUtensorMap *m, const void *B, bool bf16, int64_t K, int64_t N, int64_t ldb) {
+// TF32 B (K x N f32, row pitch ldb elements) as a 4-D map whose box is one CTA's 128-column B
+// tile in the k-group-major tiling of BTileMN<4> (tf_ptx.cuh): dims (32 columns of a 128-B
+// block, 4 rows of a k-group, column blocks, k-groups) with byte strides (-, 4 ldb, 128,
+// 16 ldb); the box is one block wide, one group high, the tile's 4 blocks and a stage's 8 groups
+// deep.  Needs N % 32 == 0 and K % 4 == 0, so that no element of a box lies outside B (the
+// per-dimension bounds cannot see a partial block or group); k-groups past K read as zero.
+int make_tmap_b_atoms(CUtensorMap *m, const void *B, int64_t K, int64_t N, int64_t ldb) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     g_last_error = "cuTensorMapEncodeTiled unavailable";
     return TFORGE_ERR_CUDA;
   }
-  const int esz = bf16 ? 2 : 4;
-  const uint32_t blk = 128 / esz, rows = bf16 ? 8 : 4, bk = 128 / esz;
-  cuuint64_t dims[4] = {blk, rows, (cuuint64_t)(N / blk), (cuuint64_t)(K / rows)};
-  cuuint64_t strides[3] = {(cuuint64_t)(ldb * esz), 128, (cuuint64_t)(rows * ldb * esz)};
-  cuuint32_t box[4] = {blk, rows, 128 / blk, bk / rows};
+  cuuint64_t dims[4] = {32, 4, (cuuint64_t)(N / 32), (cuuint64_t)(K / 4)};
+  cuuint64_t strides[3] = {(cuuint64_t)(ldb * 4), 128, (cuuint64_t)(16 * ldb)};
+  cuuint32_t box[4] = {32, 4, 4, 8};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
-                   const_cast<void *>(B), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   bf16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void *>(B), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     g_last_error = "cuTensorMapEncodeTiled failed for the 4-D B map (" + std::to_string((int)r) + ")";
@@ -489,7 +486,7 @@ int run_tc(const tforge_gemm_args *a, const TcConfig &cfg, const void *A, const 
   // tforge_config.b_layout = 3.
   if (!bkm && cfg.prec == PREC_TF32 && ((cfg.pair && cfg.bn == 256) || cfg.persist) && b_layout != 3 &&
       a->N % 32 == 0 && a->K % 4 == 0) {
-    rc = make_tmap_b_atoms(&tmB, B, bf16, a->K, a->N, ldb);
+    rc = make_tmap_b_atoms(&tmB, B, a->K, a->N, ldb);
     if (rc) return rc;
     p.b_atoms = 1;
   }
