@@ -587,6 +587,36 @@ def test_tf32_b_tile_layouts_bitwise(gpu, workload, cfg, shape):
     assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
 
 
+@pytest.mark.parametrize("persistent", [0, 1], ids=["pair", "persistent"])
+def test_tf32_b_tile_layouts_pitched_b(gpu, persistent):
+    """The k-group-major B map takes B's row pitch in two of its strides: B in a wider buffer
+    (ldb = N + 4) gives the same bits through both tilings and stays within the TF32 bound."""
+    import torch
+
+    m, n, k = 1000, 1024, 776
+    ins = tc.make_inputs("mbr", m, n, k, 57)
+    dev = torch.device("cuda", 0)
+    a = torch.from_numpy(ins["a"]).to(dev)
+    bbig = torch.full((k, n + 4), float("nan"), device=dev)  # the pitch padding is never read
+    bbig[:, :n] = torch.from_numpy(ins["b"]).to(dev)
+    bias = torch.from_numpy(ins["bias"]).to(dev)
+    outs = []
+    for layout in (1, 3):
+        out = torch.full((m, n), float("nan"), device=dev)
+        _lib.set_config(3, 256 if not persistent else 0, 0, persistent, 1 if not persistent else 0, layout)
+        try:
+            _lib.gemm("mbr", a.data_ptr(), bbig.data_ptr(), out.data_ptr(), m, n, k, "tf32", bias=bias.data_ptr(),
+                      ldb=n + 4)
+            torch.cuda.synchronize()
+        finally:
+            _lib.set_config()
+        assert _lib.device_status(None) == _lib.OK
+        outs.append(out.cpu().numpy())
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    res = tc.check_output("mbr", ins, outs[0], "tf32")
+    assert res["nan_count"] == 0 and res["err_over_bound"] <= 1.0, res
+
+
 def _bf16_rne_bits(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even f32 -> bf16 bit patterns (NaNs left to the caller)."""
     u = x.view(np.uint32).astype(np.uint64)
