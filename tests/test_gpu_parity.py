@@ -565,14 +565,14 @@ def test_tf32_transposed_b_within_bound_and_bitwise(gpu, workload, cfg, shape):
 @pytest.mark.parametrize("workload", ["mbr", "matmul", "matmul_add"])
 @pytest.mark.parametrize("cfg", [(3, 256, 0, 0, 1), (3, 0, 0, 1, 0), (3, 256, 0, 0, 3)],
                          ids=["pair", "persistent", "pair-split3"])
-@pytest.mark.parametrize("shape", [(700, 2080, 520), (2600, 1024, 264), (300, 4096, 1028)],
+@pytest.mark.parametrize("shape", [(700, 2080, 520), (2600, 1024, 264), (300, 4096, 1028), (384, 96, 200)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_tf32_b_tile_layouts_bitwise(gpu, workload, cfg, shape):
     """TF32, B as given, loaded as k-group-major tiles (the default where N and K allow it, one
     4-D box per tile) or in 128-byte column blocks (b_layout = 3): the tensor core reads the
     same values in the same order, so the results are the same bits, and within the TF32
-    bound; ragged M, N a multiple of 32 but not of the tile width, K tails, every epilogue,
-    split-K."""
+    bound; ragged M, N a multiple of 32 but not of the tile width (down to fewer column blocks
+    than one tile's box holds), K tails, every epilogue, split-K."""
     m, n, k = shape
     ins = tc.make_inputs(workload, m, n, k, 53)
     outs = []
